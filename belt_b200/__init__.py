@@ -1,0 +1,16 @@
+"""belt_b200: the latent-KV decode hot path of BELT, written for B200 (sm_100a).
+
+Modules:
+  export_latent   the latent export format (row layout, column runs, RoPE change of basis, tensors)
+  layer           ``LatentLayer`` and ``derive_latent_tensors`` (load-time constants)
+  decode          split-KV schedule, decode kernel, segment merge (``vllm_lrkv.cute_decode`` surface)
+  latent_ops      absorbed query, V up-projection, cache write (``vllm_lrkv.latent_ops`` surface)
+  latent_backend  the ``LRKV_LATENT`` attention backend (``vllm_lrkv.latent_backend`` surface)
+  dp              data-parallel partitioning of sequences across GPUs
+  synth           seeded synthetic workloads of the benchmark configurations
+  build           in-tree nvcc build of ``libbelt_b200.so``
+
+The CUDA library is loaded on first use; without it every operator raises.
+"""
+
+__version__ = "0.1.0"

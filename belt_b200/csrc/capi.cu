@@ -1,0 +1,309 @@
+// The C ABI (include/belt_b200.h): argument checks, TMA descriptor encoding and kernel launches.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/belt_b200.h"
+#include "common.cuh"
+#include "launch.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BELT_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int ok() {
+  g_last_error.clear();
+  return BELT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// BF16 tiled map with 128-byte swizzle; dims / strides innermost first (strides in bytes, rank - 1 of them).
+int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                const cuuint32_t* box, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(BELT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old?)");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BELT_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", what, (int)r);
+  return BELT_OK;
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* belt_last_error(void) { return g_last_error.c_str(); }
+
+int belt_abi_version(void) { return 100; }
+
+int belt_num_sms(int32_t device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  return n;
+}
+
+int belt_decode_schedule(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                         int32_t* work, int64_t work_capacity, int32_t* cta_seg, int32_t* seg_base, int32_t* err,
+                         void* stream) {
+  if (num_reqs < 0 || num_ctas < 1) return fail(BELT_ERR_INVALID, "schedule: num_reqs %d, num_ctas %d", num_reqs, num_ctas);
+  if ((num_reqs > 0 && !seq_lens) || !work || !cta_seg || !seg_base)
+    return fail(BELT_ERR_INVALID, "schedule: null buffer");
+  if (work_capacity < static_cast<int64_t>(num_reqs) + num_ctas)
+    return fail(BELT_ERR_INVALID, "schedule: work capacity %lld < num_reqs + num_ctas = %lld",
+                (long long)work_capacity, (long long)num_reqs + num_ctas);
+  belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, work, work_capacity, cta_seg,
+                         seg_base, err};
+  cudaError_t e = belt::launch_schedule(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "schedule launch");
+}
+
+int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64_t q_sh, const void* qmap,
+                          int32_t kq, const int32_t* col_runs, void* q_bd, void* stream) {
+  if (num_tokens < 0 || kq <= 0 || !col_runs) return fail(BELT_ERR_INVALID, "block_diag_query: bad arguments");
+  if (num_tokens == 0) return ok();
+  if (!q || !qmap || !q_bd) return fail(BELT_ERR_INVALID, "block_diag_query: null buffer");
+  belt::GroupGemmParams p{};
+  p.X = static_cast<const __nv_bfloat16*>(q);
+  p.sxt = q_st;
+  p.sxh = q_sh;
+  p.W = static_cast<const __nv_bfloat16*>(qmap);
+  p.swg = static_cast<long long>(belt::kD) * kq;
+  p.swk = kq;
+  p.swn = 1;
+  p.Out = static_cast<__nv_bfloat16*>(q_bd);
+  p.sot = static_cast<long long>(belt::kH) * kq;
+  p.soh = kq;
+  p.T = static_cast<int>(num_tokens);
+  p.K = belt::kD;
+  p.N = kq;
+  p.hpg = belt::kHPG;
+  p.G = belt::kG;
+  for (int g = 0; g < belt::kG; ++g) {
+    p.nruns[g] = 3;
+    for (int i = 0; i < 3; ++i) {
+      const int lo = col_runs[(g * 3 + i) * 2], hi = col_runs[(g * 3 + i) * 2 + 1];
+      if (lo < 0 || hi < lo || hi > kq) return fail(BELT_ERR_INVALID, "block_diag_query: column run [%d, %d) of group %d", lo, hi, g);
+      p.run_lo[g][i] = lo;
+      p.run_hi[g][i] = hi;
+    }
+  }
+  cudaError_t e = belt::launch_group_gemm(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "block_diag_query launch");
+}
+
+int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_sh, int32_t r_v, const void* v_up_t,
+                    void* out, int64_t out_st, int64_t out_sh, void* stream) {
+  if (num_tokens < 0 || r_v <= 0) return fail(BELT_ERR_INVALID, "up_project: bad arguments");
+  if (num_tokens == 0) return ok();
+  if (!a || !v_up_t || !out) return fail(BELT_ERR_INVALID, "up_project: null buffer");
+  belt::GroupGemmParams p{};
+  p.X = static_cast<const __nv_bfloat16*>(a);
+  p.sxt = a_st;
+  p.sxh = a_sh;
+  p.W = static_cast<const __nv_bfloat16*>(v_up_t);
+  p.swg = static_cast<long long>(r_v) * belt::kD;
+  p.swk = belt::kD;
+  p.swn = 1;
+  p.Out = static_cast<__nv_bfloat16*>(out);
+  p.sot = out_st;
+  p.soh = out_sh;
+  p.T = static_cast<int>(num_tokens);
+  p.K = r_v;
+  p.N = belt::kD;
+  p.hpg = belt::kHPG;
+  p.G = belt::kG;
+  for (int g = 0; g < belt::kG; ++g) {
+    p.nruns[g] = 1;
+    p.run_lo[g][0] = 0;
+    p.run_hi[g][0] = belt::kD;
+  }
+  cudaError_t e = belt::launch_group_gemm(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "up_project launch");
+}
+
+int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, const void* slots, int32_t slots_i64,
+                              void* cache, int64_t num_blocks, int32_t page, int32_t row_width, int64_t stride_block,
+                              int64_t stride_tok, const void* u_cat, int32_t lk, const int32_t* k_segs, float eps,
+                              void* stream) {
+  if (num_tokens < 0 || page <= 0 || row_width <= 0 || lk < 0 || lk > row_width || !k_segs || num_blocks < 0)
+    return fail(BELT_ERR_INVALID, "latent_rows_to_cache: bad arguments");
+  if (num_tokens == 0) return ok();
+  if (!c || !slots || !cache || !u_cat) return fail(BELT_ERR_INVALID, "latent_rows_to_cache: null buffer");
+  belt::CacheWriteParams p{};
+  p.c = static_cast<const __nv_bfloat16*>(c);
+  p.sct = c_st;
+  p.slots = slots;
+  p.slots_i64 = slots_i64 ? 1 : 0;
+  p.cache = static_cast<__nv_bfloat16*>(cache);
+  p.sblk = stride_block;
+  p.stok = stride_tok;
+  p.page = page;
+  p.W = row_width;
+  p.lk = lk;
+  p.T = static_cast<int>(num_tokens);
+  p.G = belt::kG;
+  p.num_slots = num_blocks * page;
+  p.u_cat = static_cast<const __nv_bfloat16*>(u_cat);
+  p.eps = eps;
+  for (int g = 0; g < belt::kG; ++g) {
+    p.a_lo[g] = k_segs[4 * g];
+    p.a_n[g] = k_segs[4 * g + 1];
+    p.b_lo[g] = k_segs[4 * g + 2];
+    p.b_n[g] = k_segs[4 * g + 3];
+    const int r = p.a_n[g] + p.b_n[g];
+    if (p.a_lo[g] < 0 || p.b_lo[g] < 0 || p.a_n[g] < 0 || p.b_n[g] < 0 || r > 256 ||
+        p.a_lo[g] + p.a_n[g] > lk || (p.b_n[g] > 0 && p.b_lo[g] + p.b_n[g] > lk))
+      return fail(BELT_ERR_INVALID, "latent_rows_to_cache: k_segs of group %d out of range (lk %d)", g, lk);
+  }
+  cudaError_t e = belt::launch_cache_write(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
+}
+
+int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                       int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                       const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* work,
+                       const int32_t* cta_seg, int32_t num_ctas, float* part, int64_t part_ss, int64_t part_sh,
+                       float sm_scale, int32_t lk_pad, int32_t lv, const int32_t* rope_groups,
+                       const void* rope_blocks, int32_t n_rope_blocks, const void* cos_sin, int32_t max_pos,
+                       int32_t* err, void* stream) {
+  using namespace belt;
+  if (num_reqs < 0 || num_ctas < 1) return fail(BELT_ERR_INVALID, "latent_decode: num_reqs %d, num_ctas %d", num_reqs, num_ctas);
+  if (num_reqs == 0) return ok();
+  if (!q_bd || !cache || !block_table || !seq_lens || !work || !cta_seg || !part || !rope_groups || !rope_blocks ||
+      !cos_sin)
+    return fail(BELT_ERR_INVALID, "latent_decode: null buffer");
+  const int n_k = (lk_pad + 63) / 64;
+  if (lk_pad <= 0 || lk_pad % 8 || n_k + kG > kDecodeMaxQChunks)
+    return fail(BELT_ERR_INVALID, "latent_decode: lk_pad %d must be a positive multiple of 8 and at most %d", lk_pad,
+                (kDecodeMaxQChunks - kG) * 64);
+  if (kq != n_k * 64 + kG * kRot) return fail(BELT_ERR_INVALID, "latent_decode: kq %d != n_k * 64 + 256 = %d", kq, n_k * 64 + 256);
+  if (lv <= 0 || lv > 128 * kDecodeMaxVPairs) return fail(BELT_ERR_INVALID, "latent_decode: lv %d outside (0, 640]", lv);
+  if (lk_pad + lv > row_width) return fail(BELT_ERR_INVALID, "latent_decode: lk_pad + lv %d > row width %d", lk_pad + lv, row_width);
+  if (!(page == 16 || page == 32 || page == 64 || (page % 128 == 0 && page > 0)))
+    return fail(BELT_ERR_INVALID, "latent_decode: page size %d (supported: 16, 32, 64 or a multiple of 128)", page);
+  if (num_blocks < 1 || num_blocks > (1ll << 31) - 2) return fail(BELT_ERR_INVALID, "latent_decode: num_blocks %lld", (long long)num_blocks);
+  if (!aligned16(cache) || stride_tok % 8 || stride_block % 8 || stride_tok < row_width)
+    return fail(BELT_ERR_INVALID, "latent_decode: cache rows must be 16-byte aligned (strides %lld, %lld)",
+                (long long)stride_block, (long long)stride_tok);
+  if (!aligned16(q_bd) || !aligned16(cos_sin) || !aligned16(rope_blocks))
+    return fail(BELT_ERR_INVALID, "latent_decode: q_bd, cos_sin and rope_blocks must be 16-byte aligned");
+  if (part_sh < lv + 1 || part_ss < 24 * part_sh) return fail(BELT_ERR_INVALID, "latent_decode: part strides");
+  if (max_pos < 1) return fail(BELT_ERR_INVALID, "latent_decode: max_pos %d", max_pos);
+
+  DecodeParams p{};
+  p.block_table = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.work = work;
+  p.cta_seg = cta_seg;
+  p.rope_blocks = static_cast<const __nv_bfloat16*>(rope_blocks);
+  p.rope_ld = n_rope_blocks * 64;
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+  p.max_pos = max_pos;
+  p.part = part;
+  p.part_ss = part_ss;
+  p.part_sh = part_sh;
+  p.err = err;
+  p.num_reqs = num_reqs;
+  p.num_blocks = static_cast<int>(num_blocks);
+  p.page = page;
+  p.box_rows = page < 128 ? page : 128;
+  p.n_pieces = 128 / p.box_rows;
+  p.n_k = n_k;
+  p.n_kp = (n_k + 1) / 2;
+  p.v_offset = lk_pad;
+  p.r_v = lv;
+  p.n_vp = (lv + 127) / 128;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  // rebuild K-steps: 16-column steps covering every group's [off, off + rr), read from its rope blocks
+  int nb_first = 0, nk = 0;
+  for (int g = 0; g < kG; ++g) {
+    const int off = rope_groups[2 * g], rr = rope_groups[2 * g + 1];
+    if (rr <= 0 || rr > kRot || off < 0 || off + rr > lk_pad)
+      return fail(BELT_ERR_INVALID, "latent_decode: rope group %d (%d, %d) outside the K part", g, off, rr);
+    const int c_lo = off / 64, c_hi = (off + rr - 1) / 64;
+    for (int ks = off / 16; ks <= (off + rr - 1) / 16; ++ks) {
+      if (nk >= kDecodeMaxKsteps) return fail(BELT_ERR_INVALID, "latent_decode: too many rebuild K-steps");
+      const int col = 16 * ks;
+      p.kst_col[nk] = col;
+      p.kst_src[nk] = (nb_first + (col / 64 - c_lo)) * 64 + col % 64;
+      p.kst_group[nk] = g;
+      p.kst_first[nk] = ks == off / 16;
+      ++nk;
+    }
+    nb_first += c_hi - c_lo + 1;
+  }
+  if (nb_first != n_rope_blocks)
+    return fail(BELT_ERR_INVALID, "latent_decode: %d rope blocks given, the groups need %d", n_rope_blocks, nb_first);
+  p.n_kst = nk;
+
+  CUtensorMap tm_cache, tm_q;
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_width), static_cast<cuuint64_t>(page),
+                          static_cast<cuuint64_t>(num_blocks)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_tok) * 2, static_cast<cuuint64_t>(stride_block) * 2};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(p.box_rows), 1};
+    int r = encode_bf16(&tm_cache, cache, 3, dims, strides, box, "cache");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(kq), static_cast<cuuint64_t>(num_reqs) * kH};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(kq) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kH)};
+    int r = encode_bf16(&tm_q, q_bd, 2, dims, strides, box, "q_bd");
+    if (r != BELT_OK) return r;
+  }
+  cudaError_t e = launch_latent_decode(tm_cache, tm_q, p, num_ctas, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
+}
+
+int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
+                        int32_t num_reqs, int32_t nh, int32_t lv, void* out, int64_t out_sb, int64_t out_sh,
+                        float* lse, int64_t lse_sb, void* stream) {
+  if (num_reqs < 0 || nh <= 0 || lv <= 0 || lv > 1024) return fail(BELT_ERR_INVALID, "merge_segments: bad arguments");
+  if (num_reqs == 0) return ok();
+  if (!part || !seg_base || !out || !lse) return fail(BELT_ERR_INVALID, "merge_segments: null buffer");
+  belt::MergeParams p{part, part_ss, part_sh, seg_base, num_reqs, nh, lv, static_cast<__nv_bfloat16*>(out),
+                      out_sb, out_sh, lse, lse_sb};
+  cudaError_t e = belt::launch_merge(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "merge_segments launch");
+}
+
+}  // extern "C"

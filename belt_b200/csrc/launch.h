@@ -1,0 +1,95 @@
+// Kernel parameter blocks and launchers shared by the kernels and the C-ABI layer (capi.cu).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace belt {
+
+constexpr int kDecodeMaxKsteps = 20;   // rebuild K-steps: <= 5 per group (64 coordinates at any 16-column offset)
+constexpr int kDecodeMaxVPairs = 5;    // O^T blocks of 128 latent columns: r_v <= 640
+constexpr int kDecodeMaxQChunks = 16;  // n_k + 4 query chunks of 64 columns: v_offset <= 768
+
+struct DecodeParams {
+  const int32_t* block_table;
+  long long bt_stride;
+  const int32_t* seq_lens;
+  const int32_t* work;
+  const int32_t* cta_seg;
+  const __nv_bfloat16* rope_blocks;   // [64, rope_ld]
+  int rope_ld;
+  const __nv_bfloat16* cos_sin;       // [max_pos, 64]
+  int max_pos;
+  float* part;
+  long long part_ss, part_sh;
+  int* err;
+  int num_reqs;
+  int num_blocks, page, box_rows, n_pieces;
+  int n_k, n_kp, v_offset, r_v, n_vp;
+  int n_kst;
+  int kst_col[kDecodeMaxKsteps];
+  int kst_src[kDecodeMaxKsteps];
+  int kst_group[kDecodeMaxKsteps];
+  int kst_first[kDecodeMaxKsteps];
+  float scale_log2;
+};
+
+cudaError_t launch_latent_decode(const CUtensorMap& tm_cache, const CUtensorMap& tm_q, const DecodeParams& p,
+                                 int num_ctas, cudaStream_t stream);
+int decode_smem_bytes();
+
+// Out[t, g * hpg + j, n] = X[t, g * hpg + j, :] @ W[g, :, n] for n in the group's column runs, 0 elsewhere.
+struct GroupGemmParams {
+  const __nv_bfloat16* X;
+  long long sxt, sxh;
+  const __nv_bfloat16* W;
+  long long swg, swk, swn;
+  __nv_bfloat16* Out;
+  long long sot, soh;
+  int T, K, N, hpg, G;
+  int nruns[4];
+  int run_lo[4][3], run_hi[4][3];
+};
+cudaError_t launch_group_gemm(const GroupGemmParams& p, cudaStream_t stream);
+
+struct ScheduleParams {
+  const int32_t* seq_lens;
+  int num_reqs, num_ctas, min_tiles, tile;
+  int32_t* work;
+  long long work_capacity;
+  int32_t* cta_seg;
+  int32_t* seg_base;
+  int* err;
+};
+cudaError_t launch_schedule(const ScheduleParams& p, cudaStream_t stream);
+
+struct MergeParams {
+  const float* part;
+  long long ps, ph;
+  const int32_t* seg_base;
+  int num_reqs, nh, lv;
+  __nv_bfloat16* out;
+  long long sob, soh;
+  float* lse;
+  long long slb;
+};
+cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream);
+
+struct CacheWriteParams {
+  const __nv_bfloat16* c;
+  long long sct;
+  const void* slots;
+  int slots_i64;
+  __nv_bfloat16* cache;
+  long long sblk, stok;
+  int page, W, lk, T, G;
+  long long num_slots;
+  const __nv_bfloat16* u_cat;   // [lk, G * 256]
+  int a_lo[4], a_n[4], b_lo[4], b_n[4];
+  float eps;
+};
+cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
+
+}  // namespace belt

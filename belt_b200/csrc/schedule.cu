@@ -1,0 +1,110 @@
+// Split-KV work schedule of one decode step, computed on the device (graph-safe: fixed grid, persistent buffers).
+//
+// Same split as the reference's ``_schedule`` (plugins/vllm_lrkv/vllm_lrkv/cute_decode.py:571-607): every request's
+// context is cut into `tile`-token tiles, the tiles of the whole batch (request order) are dealt out in equal runs of
+// per = max(ceil(total / num_ctas), min_tiles, 1) tiles to the CTAs, and a run that crosses request boundaries
+// becomes several segments:
+//   work[k]     = (request, first tile, end tile, 0), segments in request order;
+//   seg_base[b] = first segment of request b, seg_base[B] = number of segments;
+//   cta_seg[c]  = first segment of CTA c, cta_seg[num_ctas] = number of segments.
+// One CTA of 1024 threads; requests are processed in chunks of 1024 with block-wide exclusive scans.
+#include "common.cuh"
+#include "launch.h"
+
+namespace belt {
+
+namespace {
+constexpr int kSchedThreads = 1024;
+
+// Block-wide exclusive scan of one value per thread; returns this thread's prefix and writes the total.
+__device__ long long block_exclusive_scan(long long v, long long* warp_sums, long long* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  long long x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    long long s = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    warp_sums[lane] = s;   // inclusive over warps
+    if (lane == 31) *total = s;
+  }
+  __syncthreads();
+  const long long before = (w > 0 ? warp_sums[w - 1] : 0) + x - v;
+  __syncthreads();
+  return before;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleParams p) {
+  __shared__ long long warp_sums[32];
+  __shared__ long long total_s;
+  const int B = p.num_reqs;
+  const int tile = p.tile;
+  // pass 1: first global tile of every request (kept in seg_base until pass 2 overwrites it)
+  long long carry = 0;
+  for (int b0 = 0; b0 < B; b0 += kSchedThreads) {
+    const int b = b0 + threadIdx.x;
+    const long long tiles = b < B ? (static_cast<long long>(p.seq_lens[b]) + tile - 1) / tile : 0;
+    const long long ex = block_exclusive_scan(tiles, warp_sums, &total_s);
+    if (b < B) p.seg_base[b] = static_cast<int32_t>(carry + ex);
+    carry += total_s;
+    __syncthreads();
+  }
+  const long long total_tiles = carry;
+  long long per = (total_tiles + p.num_ctas - 1) / p.num_ctas;
+  per = per > p.min_tiles ? per : p.min_tiles;
+  per = per > 1 ? per : 1;
+  // pass 2: segments
+  long long seg_carry = 0;
+  for (int b0 = 0; b0 < B; b0 += kSchedThreads) {
+    const int b = b0 + threadIdx.x;
+    long long tiles = 0, first = 0, nseg = 0;
+    if (b < B) {
+      tiles = (static_cast<long long>(p.seq_lens[b]) + tile - 1) / tile;
+      first = p.seg_base[b];
+      nseg = tiles > 0 ? (first + tiles - 1) / per - first / per + 1 : 0;
+    }
+    const long long base = seg_carry + block_exclusive_scan(nseg, warp_sums, &total_s);
+    if (b < B) {
+      p.seg_base[b] = static_cast<int32_t>(base);
+      const long long cta0 = first / per;
+      for (long long j = 0; j < nseg; ++j) {
+        const long long cta = cta0 + j;
+        const long long g0 = first > cta * per ? first : cta * per;
+        const long long e = first + tiles;
+        const long long g1 = e < (cta + 1) * per ? e : (cta + 1) * per;
+        const long long k = base + j;
+        if (k < p.work_capacity) {
+          p.work[4 * k + 0] = b;
+          p.work[4 * k + 1] = static_cast<int32_t>(g0 - first);
+          p.work[4 * k + 2] = static_cast<int32_t>(g1 - first);
+          p.work[4 * k + 3] = 0;
+        } else if (p.err) {
+          atomicCAS(p.err, 0, kErrBadSegment);
+        }
+        if (g0 == cta * per && cta <= p.num_ctas) p.cta_seg[cta] = static_cast<int32_t>(k);
+      }
+    }
+    seg_carry += total_s;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) p.seg_base[B] = static_cast<int32_t>(seg_carry);
+  for (int c = threadIdx.x; c <= p.num_ctas; c += kSchedThreads)
+    if (static_cast<long long>(c) * per >= total_tiles) p.cta_seg[c] = static_cast<int32_t>(seg_carry);
+}
+
+cudaError_t launch_schedule(const ScheduleParams& p, cudaStream_t stream) {
+  schedule_kernel<<<1, kSchedThreads, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace belt

@@ -1,0 +1,319 @@
+"""``LRKV_LATENT``: the attention backend over the latent KV cache of ``latent`` exports, with the decode path on this
+package's sm_100a kernels. Mirrors the reference's ``vllm_lrkv.latent_backend``
+(plugins/vllm_lrkv/vllm_lrkv/latent_backend.py): same classes, constructor arguments, ``forward`` /
+``do_kv_cache_update`` signatures, metadata fields and error behaviour.
+
+Every compressed layer keeps one BF16 row per token in its own page (``LatentKVSpec``: one head slot of ``row_width``
+elements, no separate V). The model hands the op the normed, rotated query ([T, H, head_dim]), the latent projection
+of every new token as the "key" and the positions as the "value". The op first writes the tokens' cache rows
+(``latent_ops.latent_rows_to_cache``; on a second stream when the step has ``SIDE_STREAM_MIN_DECODES`` decodes or
+more, joined before the decode reads the cache), then:
+
+* decode (one query token per request, at the front of the batch): the block-diagonal query, the split-KV decode
+  kernel over the paged rows on the step's schedule (computed once per step by the builder and shared by all layers),
+  the merge of each request's segments and the per-head V up-projection written straight into ``output``;
+* prefill (everything else): rows gathered through the block table, keys and values rebuilt with
+  ``LatentLayer.decompress`` and causal attention with ``torch.nn.functional.scaled_dot_product_attention``, chunked
+  with a log-sum-exp merge beyond ``PREFILL_CHUNK`` context tokens. Prefill is not the accelerated path.
+
+The classes do not depend on vLLM: ``register_with_vllm`` installs them into a vLLM that provides the plugin API.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+import os
+from typing import ClassVar
+
+import torch
+import torch.nn.functional as F
+
+from . import decode as dec
+from . import latent_ops
+from .layer import LatentLayer
+
+BACKEND_NAME = "LRKV_LATENT"
+PREFILL_CHUNK = int(os.environ.get("LRKV_PREFILL_CHUNK_TOKENS", 32768))
+SIDE_STREAM_MIN_DECODES = int(os.environ.get("LRKV_SIDE_STREAM_MIN_DECODES", 32))
+
+
+class AttentionType:
+    DECODER = "decoder"
+    ENCODER = "encoder"
+    ENCODER_ONLY = "encoder_only"
+    ENCODER_DECODER = "encoder_decoder"
+
+
+@dataclass(frozen=True)
+class MultipleOf:
+    base: int
+
+
+@dataclass(frozen=True, kw_only=True)
+class LatentKVSpec:
+    """One compressed layer's cache: a single head slot of ``head_size`` (the row width) elements per token and no
+    separate V (latent_backend.py:57-62)."""
+
+    block_size: int
+    num_kv_heads: int = 1
+    head_size: int = 0
+    dtype: torch.dtype = torch.bfloat16
+    head_size_v: int = 0
+
+    @property
+    def page_size_bytes(self) -> int:
+        return self.block_size * self.num_kv_heads * self.head_size * torch.finfo(self.dtype).bits // 8
+
+
+@dataclass
+class CommonAttentionMetadata:
+    """The per-step batch description the builder consumes (the fields of vLLM's ``CommonAttentionMetadata`` that the
+    reference's builder reads)."""
+
+    query_start_loc: torch.Tensor           # [num_reqs + 1] int32, device
+    query_start_loc_cpu: torch.Tensor       # [num_reqs + 1] int32, host
+    seq_lens: torch.Tensor                  # [num_reqs] int32, device (this step's tokens included)
+    block_table_tensor: torch.Tensor        # [num_reqs, max_blocks] int32
+    slot_mapping: torch.Tensor              # [num_actual_tokens] int64 / int32
+    num_reqs: int
+    num_actual_tokens: int
+    max_query_len: int = 1
+    seq_lens_cpu_upper_bound: torch.Tensor | None = None
+
+
+def split_decodes_and_prefills(cm: CommonAttentionMetadata, decode_threshold: int = 1):
+    """(num_decodes, num_prefills, num_decode_tokens, num_prefill_tokens) of a batch reordered with its decode requests
+    (query length <= decode_threshold) first (vLLM's ``split_decodes_and_prefills``)."""
+    qsl = cm.query_start_loc_cpu
+    n = cm.num_reqs
+    if cm.max_query_len <= decode_threshold:
+        return n, 0, cm.num_actual_tokens, 0
+    q_len = (qsl[1:n + 1] - qsl[:n]).tolist()
+    nd = 0
+    while nd < n and q_len[nd] <= decode_threshold:
+        nd += 1
+    ndt = int(qsl[nd])
+    return nd, n - nd, ndt, cm.num_actual_tokens - ndt
+
+
+@dataclass
+class LatentAttentionMetadata:
+    num_actual_tokens: int
+    num_decodes: int
+    num_decode_tokens: int
+    num_prefills: int
+    num_prefill_tokens: int
+    block_table: torch.Tensor           # [num_reqs, max_blocks] int32
+    seq_lens: torch.Tensor              # [num_reqs] int32, including this step's tokens
+    sched: dec.DecodeSchedule | None    # the decode requests' work split, filled for this step
+    slot_mapping: torch.Tensor | None = None
+    prefill_cu_q: torch.Tensor | None = None
+    prefill_cu_k: torch.Tensor | None = None
+    prefill_max_q: int = 0
+    prefill_max_k: int = 0
+    prefill_q_len: list | None = None
+    prefill_seq_len: list | None = None
+
+
+_LAST_BUILD: dict = {}
+_SCHEDULES: dict = {}
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    """The device's second stream for the cache rows (created at the first such step, before any graph capture)."""
+    stream = _SIDE_STREAMS.get(device)
+    if stream is None:
+        stream = _SIDE_STREAMS[device] = torch.cuda.Stream(device)
+    return stream
+
+
+class LatentAttentionMetadataBuilder:
+    """Per-step metadata; fills the step's decode schedule once (latent_backend.py:148-225)."""
+
+    reorder_batch_threshold: int = 1
+    cudagraph_support: ClassVar[str] = "UNIFORM_SINGLE_TOKEN_DECODE"
+
+    def __init__(self, kv_cache_spec: LatentKVSpec, layer_names, vllm_config=None, device=None,
+                 max_num_batched_tokens: int = 8192):
+        self.kv_cache_spec = kv_cache_spec
+        self.layer_names = layer_names
+        self.device = torch.device(device if device is not None else "cuda")
+        self.block_size = kv_cache_spec.block_size
+        if vllm_config is not None:
+            max_num_batched_tokens = vllm_config.scheduler_config.max_num_batched_tokens
+        if self.device not in _SCHEDULES:
+            _SCHEDULES[self.device] = dec.make_schedule(max_num_batched_tokens, self.device)
+        self.sched = _SCHEDULES[self.device]
+
+    def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
+              fast_build: bool = False) -> LatentAttentionMetadata:
+        cm = common_attn_metadata
+        last = _LAST_BUILD.get(self.device)
+        if last is not None and last[0] is cm and last[1] == self.block_size:
+            return last[2]
+        m = self._build(cm)
+        _LAST_BUILD[self.device] = (cm, self.block_size, m)
+        return m
+
+    def _build(self, cm: CommonAttentionMetadata) -> LatentAttentionMetadata:
+        nd, npf, ndt, npt = split_decodes_and_prefills(cm, decode_threshold=1)
+        m = LatentAttentionMetadata(num_actual_tokens=cm.num_actual_tokens, num_decodes=nd, num_decode_tokens=ndt,
+                                    num_prefills=npf, num_prefill_tokens=npt, block_table=cm.block_table_tensor,
+                                    seq_lens=cm.seq_lens, sched=self.sched if nd else None,
+                                    slot_mapping=cm.slot_mapping)
+        if nd:
+            dec.schedule(self.sched, cm.seq_lens[:nd])
+        if npf:
+            qsl = cm.query_start_loc_cpu[nd:nd + npf + 1].to(torch.int64)
+            if cm.seq_lens_cpu_upper_bound is not None:
+                seq_cpu = cm.seq_lens_cpu_upper_bound[nd:nd + npf].to(torch.int64)
+            else:
+                seq_cpu = cm.seq_lens[nd:nd + npf].to("cpu", torch.int64)
+            m.prefill_q_len = (qsl[1:] - qsl[:-1]).tolist()
+            m.prefill_seq_len = seq_cpu.tolist()
+            m.prefill_max_q = max(m.prefill_q_len)
+            m.prefill_max_k = max(m.prefill_seq_len)
+        return m
+
+
+class LatentAttentionImpl:
+    def __init__(self, num_heads: int, head_size: int, scale: float, num_kv_heads: int | None = None,
+                 alibi_slopes: list | None = None, sliding_window: int | None = None, kv_cache_dtype: str = "auto",
+                 logits_soft_cap: float | None = None, attn_type: str = AttentionType.DECODER,
+                 kv_sharing_target_layer_name: str | None = None, **kwargs) -> None:
+        if (attn_type != AttentionType.DECODER or alibi_slopes is not None or sliding_window is not None
+                or logits_soft_cap or kv_sharing_target_layer_name is not None):
+            raise NotImplementedError("LRKV_LATENT: causal decoder self-attention only (no alibi, sliding window, "
+                                      "soft cap or KV sharing)")
+        if kv_cache_dtype not in ("auto", "bfloat16"):
+            raise NotImplementedError(f"LRKV_LATENT keeps a BF16 latent cache, not {kv_cache_dtype}")
+        self.num_heads, self.head_size, self.scale = num_heads, head_size, scale
+        self.num_kv_heads = num_kv_heads or num_heads
+        self.kv_cache_dtype = kv_cache_dtype
+
+    def do_kv_cache_update(self, layer, key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor,
+                           slot_mapping: torch.Tensor) -> None:
+        """key: the latent projection [T, pe_offset] of the new tokens, value: their positions (unused)."""
+        lat: LatentLayer = layer.latent
+        latent_ops.latent_rows_to_cache(key, slot_mapping, kv_cache[:, 0], lat.u_cat, lat.k_segs_host, lat.eps)
+
+    def forward(self, layer, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor,
+                attn_metadata: LatentAttentionMetadata, output: torch.Tensor, output_scale=None,
+                output_block_scale=None) -> torch.Tensor:
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError("LRKV_LATENT: fused output quantization")
+        if attn_metadata is None:                 # profiling run
+            return output.fill_(0)
+        m = attn_metadata
+        lat: LatentLayer = layer.latent
+        cache = kv_cache[:, 0]                    # [blocks, block_size, row_width], strided per block
+        nd = m.num_decode_tokens
+        slots = m.slot_mapping
+        side = None
+        if slots is not None and key is not None:
+            if m.num_decodes >= SIDE_STREAM_MIN_DECODES:
+                main, side = torch.cuda.current_stream(query.device), _side_stream(query.device)
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    self.do_kv_cache_update(layer, key, value, kv_cache, slots)
+            else:
+                self.do_kv_cache_update(layer, key, value, kv_cache, slots)
+        if m.num_decodes:
+            dev = query.device
+            q_bd = lat.block_diag_query(query[:nd])
+            if side is not None:
+                main.wait_stream(side)            # the step's own rows are part of the context
+            part = torch.empty(nd + m.sched.num_ctas, self.num_heads, lat.v_rank + 1, dtype=torch.float32,
+                               device=dev)
+            a = torch.empty(nd, self.num_heads, lat.v_rank, dtype=query.dtype, device=dev)
+            lse = torch.empty(nd, self.num_heads, dtype=torch.float32, device=dev)
+            dec.latent_decode(q_bd, cache, m.block_table[:nd], m.seq_lens[:nd], m.sched, part, self.scale,
+                              lat.v_offset, lat.v_rank, rope=lat.rope)
+            dec.merge_segments(part, m.sched, a, lse)
+            lat.up_project(a, output[:nd])
+        if m.num_prefills:
+            self._prefill(lat, query, output, cache, m)
+        return output
+
+    def _prefill(self, lat: LatentLayer, query: torch.Tensor, output: torch.Tensor, cache: torch.Tensor,
+                 m: LatentAttentionMetadata) -> None:
+        """Each prefill request's new tokens over its whole context (causal), keys and values decompressed from the
+        cache rows in chunks of ``PREFILL_CHUNK`` context tokens merged by log-sum-exp."""
+        nd, page = m.num_decodes, cache.shape[1]
+        hpg = self.num_heads // lat.num_kv_heads
+        tok = m.num_decode_tokens
+        for i in range(m.num_prefills):
+            b = nd + i
+            ql, L = m.prefill_q_len[i], m.prefill_seq_len[i]
+            q = query[tok:tok + ql].transpose(0, 1)                      # [H, ql, D]
+            q_pos = torch.arange(L - ql, L, device=query.device)
+            out = torch.zeros(self.num_heads, ql, lat.head_dim, dtype=torch.float32, device=query.device)
+            lse = torch.full((self.num_heads, ql), float("-inf"), device=query.device)
+            step = PREFILL_CHUNK if PREFILL_CHUNK > 0 else L
+            for c0 in range(0, L, step):
+                c1 = min(L, c0 + step)
+                pos = torch.arange(c0, c1, device=query.device)
+                rows = cache[m.block_table[b, pos // page].long(), pos % page]
+                k, v = lat.decompress(rows, pos)
+                k = k.transpose(0, 1).repeat_interleave(hpg, dim=0).float()   # [H, S, D]
+                v = v.transpose(0, 1).repeat_interleave(hpg, dim=0).float()
+                s = torch.einsum("hqd,hsd->hqs", q.float(), k) * self.scale
+                s = s.masked_fill(pos[None, None, :] > q_pos[None, :, None], float("-inf"))
+                c_lse = torch.logsumexp(s, dim=-1)
+                c_out = torch.einsum("hqs,hsd->hqd", torch.softmax(s, dim=-1).nan_to_num(0.0), v)
+                new = torch.logaddexp(lse, c_lse)
+                w_old = torch.exp(lse - new).nan_to_num(0.0)
+                w_new = torch.exp(c_lse - new).nan_to_num(0.0)
+                out = out * w_old[..., None] + c_out * w_new[..., None]
+                lse = new
+            output[tok:tok + ql] = out.transpose(0, 1).to(output.dtype)
+            tok += ql
+
+
+class LatentAttentionBackend:
+    # the op writes the rows itself; False keeps vLLM padding the slot mapping to the token count of the key
+    forward_includes_kv_cache_update: bool = False
+    accept_output_buffer: bool = True
+    supported_dtypes: ClassVar[list] = [torch.bfloat16]
+    supported_kv_cache_dtypes: ClassVar[list] = ["auto", "bfloat16"]
+
+    @staticmethod
+    def get_name() -> str:
+        return BACKEND_NAME
+
+    @staticmethod
+    def get_impl_cls() -> type[LatentAttentionImpl]:
+        return LatentAttentionImpl
+
+    @staticmethod
+    def get_builder_cls() -> type[LatentAttentionMetadataBuilder]:
+        return LatentAttentionMetadataBuilder
+
+    @staticmethod
+    def get_supported_kernel_block_sizes(kv_cache_spec=None) -> list:
+        # the decode kernel's tile is 128 tokens fetched as boxes of one page: 16, 32, 64 or a multiple of 128
+        return [16, 32, 64, MultipleOf(128)]
+
+    @classmethod
+    def supports_head_size(cls, head_size: int) -> bool:
+        return True
+
+    @classmethod
+    def supported_kv_cache_layouts(cls):
+        """Block-outermost only: the layers' row widths differ, so their pages share a block side by side."""
+        return ("BLHNC", "BLNHC")
+
+
+def register_with_vllm() -> bool:
+    """Register the backend under ``LRKV_LATENT`` when the running vLLM exposes the attention-backend registry of the
+    plugin API the reference targets (vLLM 0.32); returns False when it does not."""
+    try:
+        from vllm.v1.attention.backends.registry import AttentionBackendEnum  # type: ignore
+    except Exception:
+        return False
+    try:
+        AttentionBackendEnum.register(BACKEND_NAME, f"{__name__}.LatentAttentionBackend")
+    except Exception:
+        return False
+    return True

@@ -1,0 +1,105 @@
+"""The operators around the latent decode, the public surface of the reference's ``vllm_lrkv.latent_ops``
+(plugins/vllm_lrkv/vllm_lrkv/latent_ops.py), on this package's sm_100a kernels:
+
+* ``block_diag_query``: the normed, rotated query [T, H, D] times each KV group's map [D, n_k * 64 + G * rot] ->
+  the block-diagonal decode query [T, H, n_k * 64 + G * rot] (latent_ops.py:67-73);
+* ``up_project``: the merged latent output [T, H, r_v] times U_v of each head's group (stored transposed as
+  [G, r_v, D]) -> the attention output [T, H, D], in place (latent_ops.py:76-81);
+* ``latent_rows_to_cache``: the per-token cache rows ``[c_K / rho | 0 | c_v | 0]`` into the paged KV cache
+  (latent_ops.py:138-158).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .decode import _stream_ptr
+
+HEAD_DIM = 256
+
+
+def host_k_segs(k_segs) -> list:
+    """k_segs as a flat host list of 16 ints. A device tensor is copied to the host (a synchronisation): hot paths pass
+    the host rows (``LatentLayer.k_segs_host``)."""
+    if not isinstance(k_segs, torch.Tensor):
+        return [int(x) for row in k_segs for x in (row if isinstance(row, (list, tuple)) else [row])]
+    return [int(x) for x in k_segs.flatten().tolist()]
+
+
+def _runs_dense(kq: int, groups: int = 4):
+    return [[(0, kq), (0, 0), (0, 0)] for _ in range(groups)]
+
+
+def group_column_runs(k_segs, n_k: int, rot: int = 64) -> list:
+    """Per group the query columns its map can make non-zero: its latent column runs (``k_segs`` rows
+    (start, length, start, length)) and its RoPE chunk n_k * 64 + g * rot."""
+    flat = host_k_segs(k_segs)
+    rows = [flat[4 * g:4 * g + 4] for g in range(len(flat) // 4)]
+    runs = []
+    for g, (a, n, b, m) in enumerate(rows):
+        rope = n_k * 64 + g * rot
+        runs.append([(a, a + n), (b, b + m), (rope, rope + rot)])
+    return runs
+
+
+def block_diag_query(q: torch.Tensor, qmap: torch.Tensor, col_runs=None) -> torch.Tensor:
+    """q [T, H, D] (normed, rotated) and qmap [G, D, KQ] -> the decode kernel's block-diagonal query [T, H, KQ] (BF16,
+    FP32 accumulation). ``col_runs`` (``group_column_runs``) limits the work to the columns a group's map can make
+    non-zero; without it the full product is computed."""
+    T, Hq, D = q.shape
+    KQ = qmap.shape[-1]
+    if q.dtype != torch.bfloat16 or qmap.dtype != torch.bfloat16 or q.stride(-1) != 1 or not qmap.is_contiguous():
+        raise ValueError("block_diag_query: BF16 q with a contiguous last dim and a contiguous BF16 qmap")
+    if Hq != 24 or D != HEAD_DIM or qmap.shape[0] != 4 or qmap.shape[1] != D:
+        raise ValueError(f"block_diag_query: q {tuple(q.shape)} / qmap {tuple(qmap.shape)} (24 heads, 4 groups, 256)")
+    out = torch.empty(T, Hq, KQ, device=q.device, dtype=q.dtype)
+    runs = col_runs if col_runs is not None else _runs_dense(KQ)
+    flat = [x for g in runs for r in g for x in r]
+    _lib.call("belt_block_diag_query", q.data_ptr(), T, q.stride(0), q.stride(1), qmap.data_ptr(), KQ,
+              _lib.int_array(flat), out.data_ptr(), _stream_ptr(q.device))
+    return out
+
+
+def up_project(a: torch.Tensor, v_up_t: torch.Tensor, out: torch.Tensor) -> None:
+    """a [T, H, r_v] (merged latent output) and v_up_t [G, r_v, D] (U_v transposed) -> out [T, H, D] =
+    U_v,g(h) a(h), in place."""
+    R, D = v_up_t.shape[1], v_up_t.shape[2]
+    if a.shape[-1] != R or v_up_t.stride(2) != 1 or not v_up_t.is_contiguous():
+        raise ValueError("up_project: a [T, H, r_v] and a contiguous v_up_t [G, r_v, D]")
+    if a.stride(-1) != 1 or out.stride(-1) != 1 or out.shape[:2] != a.shape[:2] or D != HEAD_DIM:
+        raise ValueError("up_project: shapes / strides")
+    if a.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or v_up_t.dtype != torch.bfloat16:
+        raise ValueError("up_project: BF16 tensors")
+    _lib.call("belt_up_project", a.data_ptr(), a.shape[0], a.stride(0), a.stride(1), R, v_up_t.data_ptr(),
+              out.data_ptr(), out.stride(0), out.stride(1), _stream_ptr(a.device))
+
+
+def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor, u_cat: torch.Tensor,
+                         k_segs: torch.Tensor, eps: float) -> None:
+    """Write the cache rows of new tokens: c [T, >= pe_offset] (the latent projection; its first pe_offset columns are
+    [c_K | 0 | c_v | 0]) -> cache[slot] = [c_K / rho | 0 | c_v | 0] per group.
+
+    u_cat [lk, G * D] (BF16): U_g^T at the rows of the group's columns; k_segs [G, 4] int32: every group's columns as
+    two runs (start, length, start, length); cache [blocks, page, W]. Slots < 0 are padding."""
+    T = slot_mapping.shape[0]
+    if T == 0:
+        return
+    lk, ngd = u_cat.shape
+    segs = host_k_segs(k_segs)
+    ng = len(segs) // 4
+    if len(segs) != 16 or ngd != ng * HEAD_DIM:
+        raise ValueError("latent_rows_to_cache: head dim 256, 4 groups, k_segs [4, 4]")
+    W = cache.shape[-1]
+    if c.stride(-1) != 1 or cache.stride(-1) != 1 or not u_cat.is_contiguous():
+        raise ValueError("latent_rows_to_cache: contiguous rows")
+    if c.dtype != torch.bfloat16 or cache.dtype != torch.bfloat16 or u_cat.dtype != torch.bfloat16:
+        raise ValueError("latent_rows_to_cache: BF16 c, cache and u_cat")
+    if c.shape[1] < W:
+        raise ValueError(f"latent_rows_to_cache: c has {c.shape[1]} columns, the row width is {W}")
+    if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous():
+        raise ValueError("latent_rows_to_cache: contiguous int32 / int64 slot_mapping")
+    _lib.call("belt_latent_rows_to_cache", c.data_ptr(), T, c.stride(0), slot_mapping.data_ptr(),
+              int(slot_mapping.dtype == torch.int64), cache.data_ptr(), cache.shape[0], cache.shape[1], W,
+              cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk, _lib.int_array(segs), float(eps),
+              _stream_ptr(c.device))

@@ -1,0 +1,456 @@
+"""Benchmark of the latent-KV decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3|2] [--impl ours|reference]
+
+Workload (the headline configuration the north star names, per GPU): 16 compressed full-attention layers with learned
+per-layer ranks (r_k from {384, 448, 512, 576, 640}, r_v = 1024 - r_k, row width 1024), batch 128, context lengths
+log-uniform in [1k, 64k], block size 16, BF16, random-permuted block tables, one block holding all 16 layers' pages
+(block-outermost, strided per-layer views). ``--config 2`` runs the single-layer c50 case (batch 64 x 8192).
+
+A step is one decode step of the path over the batch: the split-KV schedule once, then per layer the cache write of
+the new token's row, the absorbed block-diagonal query, the decode kernel, the segment merge and the U_v
+up-projection. ``value`` is whole-job decode tokens/s (sequences x GPUs / step time, device-timed with CUDA events,
+max over ranks); the cache (tens of GB) is far larger than L2, so every step streams it from HBM. ``e2e`` runs the same
+step through the backend's public API (``LatentAttentionImpl.forward``) from pinned host buffers: this step's queries
+and latent rows are copied in and the attention outputs copied out inside the timed region.
+
+Multi-GPU: one process per GPU (torchrun), each with its own 128 sequences (weak scaling, data parallel, no
+collective on the data path; a gloo barrier and a max over ranks only bracket the timing).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from belt_b200 import decode as dec  # noqa: E402
+from belt_b200 import latent_ops, synth  # noqa: E402
+
+METRIC = "decode tokens/s/GPU and % of latent-attn roofline at 1/2/4/8 B200 (DP)"
+H, D = 24, 256
+SCALE = D ** -0.5
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=3, choices=[2, 3])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of one baseline sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def init_dist(world):
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+        return dist
+    return None
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def max_over_ranks(dist, x: float) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------------------------ workload
+def workload_spec(config: int, batch: int | None, rank: int):
+    """(layer specs, seq_lens, page, description) of this rank's share."""
+    if config == 2:
+        B = batch or 64
+        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}
+    B = batch or 128
+    ranks = synth.learned_ranks(16)
+    lens = synth.log_uniform_lengths(B, 1024, 65536, seed=synth.SEED_LENGTHS + 17 * rank)
+    specs = [synth.spec_from_ranks(rk, rv) for rk, rv in ranks]
+    return specs, [L + 1 for L in lens], 16, {
+        "workload": "config3: 16 layers, learned ranks (r_k in {384..640}, r_v = 1024 - r_k), batch 128/GPU, "
+                    "context log-uniform [1k, 64k], page 16"}
+
+
+class Workload:
+    def __init__(self, specs, seq_lens, page, device, rank):
+        from belt_b200.layer import derive_latent_tensors
+        self.device = device
+        self.L = len(specs)
+        self.B = len(seq_lens)
+        self.page = page
+        self.seq_lens_list = seq_lens
+        max_pos = max(seq_lens) + 1
+        cos_sin = synth.cos_sin_table(max_pos)
+        self.weights = [synth.make_layer(s, seed=synth.SEED_FACTORS + i) for i, s in enumerate(specs)]
+        self.layers = [derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin, device=device)
+                       for w in self.weights]
+        Ws = [w.layout["row_width"] for w in self.weights]
+        assert len(set(Ws)) == 1, "one row width per benchmark"
+        self.W = W = Ws[0]
+        bt, nb, _ = synth.block_tables(seq_lens, page, extra_blocks=4, seed=synth.SEED_CACHE + rank)
+        self.num_blocks = nb
+        self.block_table = bt.to(device)
+        self.seq_lens = torch.tensor(seq_lens, dtype=torch.int32, device=device)
+        # one block holds every layer's page side by side (block-outermost)
+        self.buf = torch.empty(nb, self.L, page, W, dtype=torch.bfloat16, device=device)
+        for l, w in enumerate(self.weights):
+            synth.fill_cache(self.buf[:, l], w.layout, self.block_table, seq_lens, seed=synth.SEED_CACHE + 101 * l + rank,
+                             poison=False)
+        self.caches = [self.buf[:, l] for l in range(self.L)]
+        gq = torch.Generator(device=device).manual_seed(synth.SEED_QUERY + rank)
+        self.q = torch.randn(self.L, self.B, H, D, generator=gq, device=device, dtype=torch.bfloat16)
+        self.c = torch.randn(self.L, self.B, W, generator=gq, device=device, dtype=torch.bfloat16)
+        for l, w in enumerate(self.weights):
+            self.c[l] *= synth.latent_columns(w.layout).to(device)
+        pos = torch.tensor(seq_lens) - 1
+        self.slots = (bt[torch.arange(self.B), pos // page].long() * page + pos % page).to(device)
+        self.sched = dec.make_schedule(self.B, device)
+        self.part = torch.empty(self.B + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
+        self.a = torch.empty(self.B, H, 640, dtype=torch.bfloat16, device=device)
+        self.lse = torch.empty(self.B, H, dtype=torch.float32, device=device)
+        self.out = torch.empty(self.L, self.B, H, D, dtype=torch.bfloat16, device=device)
+
+    # -------------------------------------------------------------------------------------------------------- step
+    def step(self, dec_events=None):
+        """One decode step over all layers through the operator API; ``dec_events`` [(start, end)] brackets every
+        decode-kernel launch."""
+        dec.schedule(self.sched, self.seq_lens)
+        for l, lat in enumerate(self.layers):
+            latent_ops.latent_rows_to_cache(self.c[l], self.slots, self.caches[l], lat.u_cat, lat.k_segs_host, lat.eps)
+            q_bd = lat.block_diag_query(self.q[l])
+            part = self.part[:, :, :lat.v_rank + 1]
+            if dec_events is not None:
+                dec_events[l][0].record()
+            dec.latent_decode(q_bd, self.caches[l], self.block_table, self.seq_lens, self.sched, part, SCALE,
+                              lat.v_offset, lat.v_rank, rope=lat.rope)
+            if dec_events is not None:
+                dec_events[l][1].record()
+            a = self.a[:, :, :lat.v_rank]
+            dec.merge_segments(part, self.sched, a, self.lse)
+            lat.up_project(a, self.out[l])
+
+    launches_per_step = property(lambda self: 1 + 5 * self.L)
+
+    # ------------------------------------------------------------------------------------------------ algorithmic units
+    def decode_kernel_bytes(self, l: int) -> int:
+        """Algorithmic bytes of one decode-kernel launch: every context row read once, the block-diagonal query."""
+        lat = self.layers[l]
+        rows = sum(self.seq_lens_list) * self.W * 2
+        kq = lat.n_k * 64 + 4 * 64
+        return rows + self.B * H * kq * 2
+
+    def step_bytes(self) -> int:
+        """Algorithmic bytes of one step (rows, factors, q in, out, new rows), summed over layers."""
+        tot = 0
+        for l, lat in enumerate(self.layers):
+            lay = self.weights[l].layout
+            rows = sum(self.seq_lens_list) * self.W * 2
+            factors = 2 * (sum(256 * r for r in lay["k_head_ranks"]) + 4 * 256 * lay["v_rank"])
+            qo = 2 * self.B * H * D * 2
+            tot += rows + factors + qo + 2 * self.B * self.W
+        return tot
+
+
+# ------------------------------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s, p in zip(sm, power) if p > 0.3 * max(power)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ------------------------------------------------------------------------------------------------------------ CPU arm
+def cpu_reference_rate(specs, seq_lens, page, budget_s: float, rank: int = 0):
+    """Decode tokens/s of the reference's torch path (the oracle port of ``LatentLayer.decompress`` + fp32 attention)
+    on this host's cores, extrapolated to the whole workload from a bounded sample of requests of the first layer.
+    Returns (tokens/s, cores, sample description, seconds)."""
+    import oracle
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w = synth.make_layer(specs[0], seed=synth.SEED_FACTORS)
+    total_ctx = sum(seq_lens)
+    # calibrate on a short request, then size the sample to the budget
+    order = sorted(range(len(seq_lens)), key=lambda i: seq_lens[i])
+    probe = [seq_lens[order[len(order) // 2]]]
+    t_probe = _cpu_time(w, probe, page)
+    per_tok = t_probe / sum(probe)
+    want = max(1, int(budget_s / per_tok))
+    sample, acc = [], 0
+    for i in order[len(order) // 4:] + order[:len(order) // 4]:
+        if acc + seq_lens[i] > want and sample:
+            break
+        sample.append(seq_lens[i])
+        acc += seq_lens[i]
+    t = _cpu_time(w, sample, page)
+    per_tok = t / sum(sample)
+    step_s = per_tok * total_ctx * len(specs)                 # every layer of every sequence
+    rate = len(seq_lens) / step_s
+    desc = (f"oracle port of the reference torch path (decompress + fp32 attention), layer 0, {len(sample)} requests "
+            f"/ {sum(sample)} context tokens timed ({t:.1f} s), extrapolated per context token to {len(specs)} layers "
+            f"x {total_ctx} tokens")
+    return rate, cores, desc, t
+
+
+def _cpu_time(w, lens, page):
+    import oracle
+    cos_sin = synth.cos_sin_table(max(lens) + 1)
+    ref = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin)
+    batch = synth.make_batch(w.layout, lens, page=page, seed=synth.SEED_CACHE, poison=False)
+    q = synth.make_queries(len(lens))
+    t0 = time.perf_counter()
+    oracle.decode_reference(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+    return time.perf_counter() - t0
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, 0)
+    rates, tsum = [], 0.0
+    for i in range(args.warmup + args.steps):
+        budget = min(args.cpu_seconds, 240.0 / max(1, args.warmup + args.steps))
+        rate, cores, desc, t = cpu_reference_rate(specs, seq_lens, page, budget)
+        if i >= args.warmup:
+            rates.append(rate)
+            tsum += t
+    value = statistics.median(rates)
+    ms = 1000.0 * len(seq_lens) / value
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {**cfg, "global_batch": len(seq_lens), "parallelism": "dp (rank 0 only: CPU)"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------------------ e2e
+def e2e_rate(wl: Workload, steps: int, warmup: int):
+    """Decode tokens/s through ``LatentAttentionImpl.forward`` with this step's inputs copied from pinned host memory
+    and the outputs copied back inside the timed region."""
+    from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl,
+                                          LatentAttentionMetadataBuilder, LatentKVSpec)
+    dev = wl.device
+    B, L = wl.B, wl.L
+    q_host = wl.q.cpu().pin_memory()
+    c_host = wl.c.cpu().pin_memory()
+    pos_host = (torch.tensor(wl.seq_lens_list) - 1).pin_memory()
+    out_host = torch.empty(L, B, H, D, dtype=torch.bfloat16).pin_memory()
+    q_dev, c_dev = torch.empty_like(wl.q), torch.empty_like(wl.c)
+    pos_dev = torch.empty(B, dtype=torch.int64, device=dev)
+    out_dev = torch.empty(L, B, H, D, dtype=torch.bfloat16, device=dev)
+    spec = LatentKVSpec(block_size=wl.page, num_kv_heads=1, head_size=wl.W)
+    builder = LatentAttentionMetadataBuilder(spec, [f"layers.{l}" for l in range(L)], device=dev,
+                                             max_num_batched_tokens=max(256, B))
+    impl = LatentAttentionImpl(H, D, SCALE, 4)
+
+    class _Layer:
+        def __init__(self, lat):
+            self.latent = lat
+    layer_objs = [_Layer(lat) for lat in wl.layers]
+    kv = wl.buf.view(wl.num_blocks, L, 1, wl.page, wl.W)
+    qsl = torch.arange(B + 1, dtype=torch.int32)
+    qsl_dev = qsl.to(dev)
+
+    def one():
+        q_dev.copy_(q_host, non_blocking=True)
+        c_dev.copy_(c_host, non_blocking=True)
+        pos_dev.copy_(pos_host, non_blocking=True)
+        cm = CommonAttentionMetadata(query_start_loc=qsl_dev, query_start_loc_cpu=qsl, seq_lens=wl.seq_lens,
+                                     block_table_tensor=wl.block_table, slot_mapping=wl.slots, num_reqs=B,
+                                     num_actual_tokens=B, max_query_len=1)
+        md = builder.build(0, cm)
+        for l in range(L):
+            impl.forward(layer_objs[l], q_dev[l], c_dev[l], pos_dev, kv[:, l], md, out_dev[l])
+        out_host.copy_(out_dev, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    h2d = q_host.numel() * 2 + c_host.numel() * 2 + pos_host.numel() * 8
+    d2h = out_host.numel() * 2
+    return B / (ms / 1000.0), ms, h2d, d2h
+
+
+def read_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary (None until captured)."""
+    path = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    dist = init_dist(world)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from belt_b200 import build as _build
+    _build.build()
+    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, rank)
+    wl = Workload(specs, seq_lens, page, dev, rank)
+    torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        wl.step()
+    torch.cuda.synchronize()
+    dec.check_device_errors(dev)
+
+    dec_events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(wl.L)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    barrier(dist)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for k in range(args.steps):
+        wl.step(dec_events[k])
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier(dist)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(dist, ms_local)
+    dec.check_device_errors(dev)
+    value = world * wl.B / (ms / 1000.0)
+
+    # the decode kernel's launches, per layer
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak_gbs = peaks.get("hbm_gbs") or 6650.0
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    kern_ms = [statistics.mean(dec_events[k][l][0].elapsed_time(dec_events[k][l][1]) for k in range(args.steps))
+               for l in range(wl.L)]
+    kern_bytes = [wl.decode_kernel_bytes(l) for l in range(wl.L)]
+    achieved = sum(kern_bytes) / (sum(kern_ms) / 1000.0) / 1e9
+    step_gb = wl.step_bytes() / 1e9
+    step_frac = step_gb / (ms / 1000.0) / peak_gbs
+    traffic = read_traffic()
+    traffic_per_launch = None
+    if traffic and traffic.get("bytes_per_context_token"):
+        traffic_per_launch = traffic["bytes_per_context_token"] * sum(wl.seq_lens_list)
+
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**cfg, "global_batch": wl.B * world, "per_gpu_batch": wl.B, "layers": wl.L,
+                       "context_tokens_per_gpu": sum(wl.seq_lens_list), "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (cache %.1f GB per GPU)" % (wl.buf.numel() * 2 / 1e9),
+                       "tokens_per_s_per_gpu": value / world,
+                       "step_roofline_frac": step_frac, "step_algorithmic_gb": step_gb},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
+                         "frac": achieved / peak_gbs, "peak_source": peak_src,
+                         "kernel": "latent_decode_kernel", "kernel_ms_per_launch": sum(kern_ms) / wl.L,
+                         "traffic": traffic_per_launch / wl.L if traffic_per_launch else None},
+            "clocks": clk,
+            "gpu_launches": wl.launches_per_step * args.steps}
+    if not args.no_e2e:
+        e_rate, e_ms, h2d, d2h = e2e_rate(wl, max(2, args.steps // 2), 2)
+        e_rate = max_over_ranks(dist, e_ms)
+        line["e2e"] = {"value": world * wl.B / (e_rate / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "ms_per_step": e_rate}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, desc, t = cpu_reference_rate(specs, seq_lens, page, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,120 @@
+/*
+ * belt_b200 — C ABI of the B200 (sm_100a) latent-KV decode path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, launches on the given CUDA stream
+ * (a cudaStream_t passed as void*, NULL = the legacy default stream), allocates nothing and returns
+ * BELT_OK or a negative status; belt_last_error() then describes the failure (thread-local). Launches are
+ * asynchronous; they can be captured in CUDA graphs. BF16 tensors are passed as `const void*` / `void*`.
+ *
+ * Each entry point replaces one operator of the reference's vLLM plugin
+ * (liuyaoyang04/BELT, plugins/vllm_lrkv/vllm_lrkv/), cited per function.
+ */
+#ifndef BELT_B200_H_
+#define BELT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BELT_OK 0
+#define BELT_ERR_INVALID (-1)     /* bad shape, stride, alignment or unsupported layout */
+#define BELT_ERR_CUDA (-2)        /* a CUDA runtime / driver call failed */
+
+/* Tokens per split-KV tile of the decode kernel (the schedule's unit). */
+#define BELT_DECODE_TILE 128
+
+/* Thread-local description of the last failure of a belt_* call on this thread ("" if none). */
+const char* belt_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+int belt_abi_version(void);
+
+/*
+ * Split-KV schedule of one decode step: replaces cute_decode.py:601-607 (`schedule`) / :571-598 (`_schedule`).
+ * seq_lens [num_reqs] int32 (device, including this step's token) -> work [work_capacity, 4] int32
+ * (request, first tile, end tile, 0) per segment, cta_seg [num_ctas + 1] int32, seg_base [num_reqs + 1] int32.
+ * Tiles are BELT_DECODE_TILE tokens; runs of max(ceil(tiles / num_ctas), min_tiles) tiles per CTA. A request of
+ * length 0 gets no segment. work_capacity >= num_reqs + num_ctas always suffices. err: optional device int32
+ * word that receives a nonzero code if the capacity is exceeded.
+ */
+int belt_decode_schedule(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                         int32_t* work, int64_t work_capacity, int32_t* cta_seg, int32_t* seg_base, int32_t* err,
+                         void* stream);
+
+/*
+ * Absorbed block-diagonal decode query: replaces latent_ops.py:67-73 (`block_diag_query`, the grouped GEMM of
+ * :23-44). q [T, 24, 256] BF16 (element strides q_st, q_sh; last dim contiguous) x qmap [4, 256, kq] BF16
+ * (contiguous) -> q_bd [T, 24, kq] BF16 (contiguous). Only the columns listed in col_runs are computed for each
+ * group (host array [4][3][2] of [start, end) runs, an empty run has start == end); the other columns are written
+ * as zeros. A qmap made by `derive_latent_tensors` is zero outside its group's latent columns and RoPE chunk, so
+ * passing those runs gives the dense product.
+ */
+int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64_t q_sh, const void* qmap,
+                          int32_t kq, const int32_t* col_runs, void* q_bd, void* stream);
+
+/*
+ * Per-head V up-projection: replaces latent_ops.py:76-81 (`up_project`). a [T, 24, r_v] BF16 (strides a_st,
+ * a_sh) x v_up_t [4, r_v, 256] BF16 (contiguous, U_v transposed) -> out [T, 24, 256] BF16 (strides out_st, out_sh),
+ * written in place (e.g. a view of the first rows of the attention output).
+ */
+int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_sh, int32_t r_v, const void* v_up_t,
+                    void* out, int64_t out_st, int64_t out_sh, void* stream);
+
+/*
+ * Latent cache write: replaces latent_ops.py:138-158 (`latent_rows_to_cache`, kernel `_latent_rows` :85-135).
+ * c [T, >= W] BF16 (row stride c_st): the latent projection of the new tokens, [c_K | 0 | c_v | 0].
+ * slots [T] int32 (slots_i64 = 0) or int64 (slots_i64 = 1); slot s goes to block s / page, row s % page;
+ * s < 0 or s >= num_blocks * page is skipped. cache: the layer's [num_blocks, page, W] BF16 view with element
+ * strides (stride_block, stride_tok, 1). u_cat [lk, 4 * 256] BF16 contiguous; k_segs: host int32 [4][4] =
+ * (start, length, start, length) per group; eps of the k_norm RMS. Writes rows [c_K / rho | c[lk:W]].
+ */
+int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, const void* slots, int32_t slots_i64,
+                              void* cache, int64_t num_blocks, int32_t page, int32_t row_width, int64_t stride_block,
+                              int64_t stride_tok, const void* u_cat, int32_t lk, const int32_t* k_segs, float eps,
+                              void* stream);
+
+/*
+ * Single-pass paged latent decode (split-KV partials): replaces cute_decode.py:649-678 (`latent_decode_cute`,
+ * kernel `LatentDecodeSm90` :90-484).
+ *   q_bd [num_reqs, 24, kq] BF16 contiguous (belt_block_diag_query), kq = n_k * 64 + 4 * 64, n_k = ceil(lk_pad / 64);
+ *   cache [num_blocks, page, W] BF16 view, element strides (stride_block, stride_tok, 1), 16-byte aligned rows;
+ *     page in {16, 32, 64} or a multiple of 128;
+ *   block_table [num_reqs, >= pages] int32 (row stride bt_stride); seq_lens [num_reqs] int32 (this step's token
+ *     included, already written);
+ *   work / cta_seg: belt_decode_schedule output for these seq_lens with num_ctas CTAs;
+ *   part [>= segments, 24, lv + 1] fp32 (element strides part_ss, part_sh; last dim contiguous): per segment the
+ *     normalised latent V-space output and the natural-log LSE of the scaled scores;
+ *   sm_scale: softmax scale (head_dim^-0.5); lk_pad = v_offset (start of the V part), lv = r_v (<= 640);
+ *   rope_groups: host int32 [4][2] = (first column, rr_g) of every group's RoPE coordinates;
+ *   rope_blocks [64, n_rope_blocks * 64] BF16 contiguous (`rope_blocks`, cute_decode.py:635-646);
+ *   cos_sin [max_pos, 64] BF16 contiguous (cos half | sin half); token t of a request sits at position t;
+ *   err: optional device int32 word receiving a nonzero code if a wait in the kernel timed out.
+ */
+int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                       int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                       const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* work,
+                       const int32_t* cta_seg, int32_t num_ctas, float* part, int64_t part_ss, int64_t part_sh,
+                       float sm_scale, int32_t lk_pad, int32_t lv, const int32_t* rope_groups,
+                       const void* rope_blocks, int32_t n_rope_blocks, const void* cos_sin, int32_t max_pos,
+                       int32_t* err, void* stream);
+
+/*
+ * Segment merge: replaces cute_decode.py:715-722 (`merge_segments`, kernel `_merge_segments` :681-712).
+ * part [segments, nh, lv + 1] fp32 (strides part_ss, part_sh), seg_base [num_reqs + 1] int32 ->
+ * out [num_reqs, nh, lv] BF16 (strides out_sb, out_sh), lse [num_reqs, nh] fp32 (row stride lse_sb).
+ * A request without segments gets zeros and -inf.
+ */
+int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
+                        int32_t num_reqs, int32_t nh, int32_t lv, void* out, int64_t out_sb, int64_t out_sh,
+                        float* lse, int64_t lse_sb, void* stream);
+
+/* Number of SMs of `device` (the decode grid: one CTA per SM). */
+int belt_num_sms(int32_t device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BELT_B200_H_ */

@@ -41,16 +41,37 @@ def golden_case(name):
     return fx, spec, w, batch, q
 
 
+class UlpCheck:
+    """Result of ``bf16_ulp_close``: truthy when every element is within the bound; ``repr`` says where it is not."""
+
+    def __init__(self, ok, msg=""):
+        self.ok, self.msg = ok, msg
+
+    def __bool__(self):
+        return self.ok
+
+    def __repr__(self):
+        return f"UlpCheck({self.ok}: {self.msg})"
+
+
 def bf16_ulp_close(a, b, ulps=1):
     """|a - b| <= ulps BF16 ulps of max(|a|, |b|) elementwise (NaN positions must agree)."""
     a, b = a.float(), b.float()
-    if not torch.equal(torch.isnan(a), torch.isnan(b)):
-        return False
-    m = ~torch.isnan(a)
+    na, nb = torch.isnan(a), torch.isnan(b)
+    if not torch.equal(na, nb):
+        idx = (na != nb).nonzero()[:5].tolist()
+        return UlpCheck(False, f"NaN positions differ ({int((na != nb).sum())}), first {idx}")
+    m = ~na
     a, b = a[m], b[m]
     mag = torch.maximum(a.abs(), b.abs())
     ulp = torch.where(mag > 0, 2.0 ** (torch.floor(torch.log2(mag.clamp_min(1e-38))) - 7), torch.zeros_like(mag))
-    return bool(((a - b).abs() <= ulps * ulp + 1e-30).all())
+    bad = (a - b).abs() > ulps * ulp + 1e-30
+    if bad.any():
+        r = ((a - b).abs() / ulp.clamp_min(1e-38))[bad]
+        i = bad.nonzero()[:3].flatten().tolist()
+        return UlpCheck(False, f"{int(bad.sum())} elements beyond {ulps} ulp (max {float(r.max()):.1f} ulp), first at "
+                               f"flat {i}: {a[i].tolist()} vs {b[i].tolist()}")
+    return UlpCheck(True)
 
 
 @pytest.fixture(scope="session")

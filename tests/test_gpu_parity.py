@@ -1,0 +1,318 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle and the reference's golden outputs.
+
+Tolerances: the schedule and the cache-row placement are compared bit for bit; cache-row values within 1 BF16 ulp
+(the reference's rsqrt and dot order are not bit-defined); the attention output within max-abs 2e-2 and mean-abs 2e-3
+of the fp32 oracle (the north-star bound for BF16).
+"""
+
+import math
+
+import pytest
+import torch
+
+import oracle
+from belt_b200 import decode as dec
+from belt_b200 import latent_ops, synth
+from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl, LatentAttentionMetadataBuilder,
+                                      LatentKVSpec)
+from belt_b200.layer import derive_latent_tensors
+
+from conftest import CASES, bf16_ulp_close, golden_case
+
+pytestmark = pytest.mark.gpu
+SCALE = 256 ** -0.5
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+DEV = "cuda"
+
+
+def layer_pair(w, max_pos=4096, device=DEV):
+    cos_sin = synth.cos_sin_table(max_pos)
+    lat = derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin, device=device)
+    ref = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin)
+    return lat, ref
+
+
+def run_decode(lat, q, cache, block_table, seq_lens, num_ctas=None):
+    """The backend's decode chain on the device; returns (out, a, lse, part, sched)."""
+    B = q.shape[0]
+    sched = dec.make_schedule(B, q.device, num_ctas=num_ctas)
+    dec.schedule(sched, seq_lens)
+    q_bd = lat.block_diag_query(q)
+    part = torch.full((B + sched.num_ctas, 24, lat.v_rank + 1), float("nan"), device=q.device)
+    dec.latent_decode(q_bd, cache, block_table, seq_lens, sched, part, SCALE, lat.v_offset, lat.v_rank, rope=lat.rope)
+    a = torch.empty(B, 24, lat.v_rank, dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty(B, 24, device=q.device)
+    dec.merge_segments(part, sched, a, lse)
+    out = torch.empty(B, 24, 256, dtype=torch.bfloat16, device=q.device)
+    lat.up_project(a, out)
+    torch.cuda.synchronize()
+    dec.check_device_errors(q.device)
+    return out, a, lse, part, sched, q_bd
+
+
+def assert_close_out(out, ref, what=""):
+    err = (out.float().cpu() - ref.float().cpu()).abs()
+    assert torch.isfinite(out.float()).all(), f"{what}: non-finite output"
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (what, float(err.max()), float(err.mean()))
+
+
+# ------------------------------------------------------------------------------------------------- schedule
+@pytest.mark.parametrize("seqs,nct", [
+    ([129, 513, 1025, 2001], 148), ([1, 17, 129, 300], 8), ([0, 64, 0, 65, 4096, 1], 16), ([8192] * 64, 148),
+    ([5], 148), ([0, 0], 4), ([3000, 1, 1, 1, 7000, 64, 63, 65], 148), ([200] * 300, 148), ([128, 256, 127], 1),
+    (list(range(0, 3000, 7)), 148),
+])
+def test_schedule_bit_exact(seqs, nct):
+    B = len(seqs)
+    sched = dec.make_schedule(B, DEV, num_ctas=nct)
+    sched.work.fill_(-7)
+    dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
+    work, cta_seg, seg_base = oracle.schedule(seqs, nct, dec.TILE_T)
+    total = int(seg_base[-1])
+    torch.cuda.synchronize()
+    assert torch.equal(sched.seg_base.cpu(), torch.from_numpy(seg_base))
+    assert torch.equal(sched.cta_seg.cpu(), torch.from_numpy(cta_seg))
+    assert torch.equal(sched.work[:total].cpu(), torch.from_numpy(work[:total]))
+
+
+# ------------------------------------------------------------------------------------------------- cache write
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
+def test_cache_write(name, slot_dtype):
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    page = fx["page"]
+    gcw = torch.Generator().manual_seed(9)
+    c = (torch.randn(24, W, generator=gcw) * synth.latent_columns(w.layout)).to(torch.bfloat16)
+    slots = fx["cw_slots"]
+    nb = fx["cw_nb"]
+    init = torch.full((nb, page, W), float("nan")).to(torch.bfloat16)
+    init.view(-1, W)[::3] = 1.5                           # some untouched rows with finite content
+    exp = oracle.latent_rows(c, slots, init.clone(), ref["u_cat"], ref["k_segs"], 1e-6)
+    cache = init.clone().to(DEV)
+    latent_ops.latent_rows_to_cache(c.to(DEV), slots.to(slot_dtype).to(DEV), cache, lat.u_cat, lat.k_segs, 1e-6)
+    torch.cuda.synchronize()
+    got = cache.cpu()
+    live = slots >= 0
+    written = slots[live].long()
+    untouched = torch.ones(nb * page, dtype=torch.bool)
+    untouched[written] = False
+    # placement: every untouched row is bit-identical, every written row lands in its slot
+    assert torch.equal(got.view(-1, W)[untouched].view(torch.int16), init.view(-1, W)[untouched].view(torch.int16))
+    assert bf16_ulp_close(got.view(-1, W)[written], exp.view(-1, W)[written], ulps=1)
+    assert bf16_ulp_close(got.view(-1, W)[written], fx["cw_rows"], ulps=1)
+
+
+def test_cache_write_strided_view_and_padding():
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    page, nb, layers = 16, 40, 3
+    buf = torch.zeros(nb, layers * page * W, dtype=torch.bfloat16, device=DEV)
+    view = buf.view(nb, layers, page, W)[:, 1]                    # the middle layer's pages, block stride 3 pages
+    T = 300
+    g = torch.Generator().manual_seed(4)
+    c = (torch.randn(T, W + 64, generator=g) * torch.cat([synth.latent_columns(w.layout), torch.ones(64)])).to(
+        torch.bfloat16)
+    slots = torch.randperm(nb * page, generator=g)[:T]
+    slots[::7] = -1
+    latent_ops.latent_rows_to_cache(c.to(DEV), slots.to(DEV), view, lat.u_cat, lat.k_segs, 1e-6)
+    exp = oracle.latent_rows(c[:, :W], slots, torch.zeros(nb, page, W, dtype=torch.bfloat16), ref["u_cat"],
+                             ref["k_segs"], 1e-6)
+    torch.cuda.synchronize()
+    full = buf.view(nb, layers, page, W).cpu()
+    assert bf16_ulp_close(full[:, 1], exp, ulps=1)
+    assert not full[:, 0].any() and not full[:, 2].any()          # neighbouring layers untouched
+
+
+# ------------------------------------------------------------------------------------------------- query / up-projection
+@pytest.mark.parametrize("name", CASES)
+def test_block_diag_query(name):
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    exp = oracle.block_diag_query(q, ref["qmap"])
+    got = lat.block_diag_query(q.to(DEV)).cpu()
+    assert bf16_ulp_close(got, exp, ulps=1)
+    assert bf16_ulp_close(got, fx["q_bd"], ulps=1)
+    dense = latent_ops.block_diag_query(q.to(DEV), lat.qmap).cpu()  # the full product gives the same query
+    assert bf16_ulp_close(dense, exp, ulps=1)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_up_project(name):
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    B = q.shape[0]
+    a = torch.randn(B, 24, spec.v_rank, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    out = torch.zeros(B + 3, 24, 256, dtype=torch.bfloat16, device=DEV)
+    lat.up_project(a.to(DEV), out[:B])
+    got = out.cpu()
+    assert bf16_ulp_close(got[:B], fx["up_out"], ulps=1)
+    assert not got[B:].any()
+
+
+def test_merge_segments():
+    g = torch.Generator().manual_seed(2)
+    for seqs, nct, lv in [([129, 513, 1025, 2001], 16, 512), ([0, 300, 64, 0], 8, 96), ([40] * 12, 8, 640),
+                          ([9000] * 3, 148, 512)]:
+        B = len(seqs)
+        sched = dec.make_schedule(B, DEV, num_ctas=nct)
+        dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
+        nseg = int(sched.seg_base[B])
+        part = torch.randn(nseg + 1, 24, lv + 1, generator=g)
+        part[:, :, lv] *= 4
+        a = torch.empty(B, 24, lv, dtype=torch.bfloat16, device=DEV)
+        lse = torch.empty(B, 24, device=DEV)
+        dec.merge_segments(part.to(DEV), sched, a, lse)
+        ea, el = oracle.merge_segments(part, sched.seg_base.cpu(), B, lv)
+        torch.cuda.synchronize()
+        assert bf16_ulp_close(a.cpu(), ea.to(torch.bfloat16), ulps=1)
+        live = torch.isfinite(el)
+        assert torch.equal(torch.isfinite(lse.cpu()), live)
+        assert torch.allclose(lse.cpu()[live], el[live], atol=1e-4)
+
+
+# ------------------------------------------------------------------------------------------------- decode
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("num_ctas", [148, 7, 1])
+def test_decode_partials(name, num_ctas):
+    """The kernel's per-segment partials against the oracle's split with the kernel's rounding points."""
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    out, a, lse, part, sched, q_bd = run_decode(lat, q.to(DEV), batch.cache.to(DEV), batch.block_table.to(DEV),
+                                               batch.seq_lens.to(DEV), num_ctas)
+    B = q.shape[0]
+    nseg = int(sched.seg_base[B])
+    exp = oracle.decode_partials(q_bd.cpu(), batch.cache, batch.block_table, batch.seq_lens, ref,
+                                 sched.work.cpu(), nseg, SCALE, dec.TILE_T)
+    got = part[:nseg].cpu()
+    assert torch.isfinite(got).all()
+    assert torch.allclose(got[:, :, -1], exp[:, :, -1], atol=2e-3, rtol=1e-4), \
+        float((got[:, :, -1] - exp[:, :, -1]).abs().max())
+    err = (got[:, :, :-1] - exp[:, :, :-1]).abs()
+    assert float(err.max()) < 2e-2 and float(err.mean()) < 2e-3, (float(err.max()), float(err.mean()))
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_decode_matches_reference_output(name):
+    """Whole decode chain vs the reference's own torch path (golden) and the fp32 oracle."""
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    out, *_ = run_decode(lat, q.to(DEV), batch.cache.to(DEV), batch.block_table.to(DEV), batch.seq_lens.to(DEV))
+    assert_close_out(out, fx["out_reference"], f"{name} vs reference")
+    exp_b = oracle.decode_fp32(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+    assert_close_out(out, exp_b, f"{name} vs fp32")
+
+
+@pytest.mark.parametrize("page", [16, 32, 64, 128, 256])
+def test_decode_page_sizes_and_strided_views(page):
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=5000)
+    seqs = [1, 127, 128, 129, 700, 4097, 0, 255]
+    layout = w.layout
+    bt, nb, owned = synth.block_tables(seqs, page, extra_blocks=3)
+    W = layout["row_width"]
+    layers = 2
+    buf = torch.empty(nb, layers, page, W, dtype=torch.bfloat16)
+    cache = buf[:, 1]                                        # strided per-layer view
+    synth.fill_cache(cache, layout, bt, seqs, seed=5)
+    buf[:, 0] = float("nan")
+    q = synth.make_queries(len(seqs), seed=6)
+    gbuf = buf.to(DEV)
+    out, *_ = run_decode(lat, q.to(DEV), gbuf[:, 1], bt.to(DEV), torch.tensor(seqs, dtype=torch.int32, device=DEV))
+    exp = oracle.decode_fp32(q, cache, bt, torch.tensor(seqs), ref, SCALE)
+    assert_close_out(out, exp, f"page {page}")
+    assert not out[6].float().abs().any()                     # a padded request (length 0) gives zeros
+
+
+def test_decode_invariances():
+    """Bit-identical under a permutation of physical blocks; within tolerance across different CTA counts."""
+    spec = synth.spec_from_ranks(448, 576)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=9000)
+    seqs = [3000, 17, 8193, 640]
+    batch = synth.make_batch(w.layout, seqs, page=16, seed=8)
+    q = synth.make_queries(len(seqs), seed=9).to(DEV)
+    o1, *_ = run_decode(lat, q, batch.cache.to(DEV), batch.block_table.to(DEV), batch.seq_lens.to(DEV), 148)
+    # move every block to a new physical position
+    nb = batch.cache.shape[0]
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(1))
+    cache2 = torch.empty_like(batch.cache)
+    cache2[perm] = batch.cache
+    bt2 = perm[batch.block_table.long()].to(torch.int32)
+    o2, *_ = run_decode(lat, q, cache2.to(DEV), bt2.to(DEV), batch.seq_lens.to(DEV), 148)
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    o3, *_ = run_decode(lat, q, batch.cache.to(DEV), batch.block_table.to(DEV), batch.seq_lens.to(DEV), 5)
+    err = (o1.float() - o3.float()).abs()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS
+    exp = oracle.decode_fp32(q.cpu(), batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+    assert_close_out(o1, exp, "ragged 448/576")
+
+
+def test_backend_forward_decode_step():
+    """The backend surface end to end: builder -> impl.forward (cache write of this step's token, then decode)."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    seqs = [40, 300, 1, 2050, 129] * 8                    # 40 decodes: the cache write runs on the side stream
+    page = 16
+    bt, nb, _ = synth.block_tables(seqs, page, extra_blocks=2)
+    W = w.layout["row_width"]
+    kv = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv[:, 0], w.layout, bt, seqs, seed=3, poison=False)
+    B = len(seqs)
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(B, w.kv_latent_proj.shape[1], generator=g).to(torch.bfloat16)
+    c = (x.float() @ w.kv_latent_proj.float().T).to(torch.bfloat16)          # the latent projection of the new token
+    pos = torch.tensor(seqs) - 1
+    slots = bt[torch.arange(B), pos // page].long() * page + pos % page
+    q = synth.make_queries(B, seed=13)
+    # expected: write the new rows on the CPU, then the fp32 oracle
+    exp_cache = oracle.latent_rows(c, slots, kv[:, 0].clone(), ref["u_cat"], ref["k_segs"], 1e-6)
+    exp = oracle.decode_fp32(q, exp_cache, bt, torch.tensor(seqs), ref, SCALE)
+
+    spec_kv = LatentKVSpec(block_size=page, num_kv_heads=1, head_size=W)
+    builder = LatentAttentionMetadataBuilder(spec_kv, ["l0"], device=DEV, max_num_batched_tokens=256)
+    cm = CommonAttentionMetadata(query_start_loc=torch.arange(B + 1, dtype=torch.int32, device=DEV),
+                                 query_start_loc_cpu=torch.arange(B + 1, dtype=torch.int32),
+                                 seq_lens=torch.tensor(seqs, dtype=torch.int32, device=DEV),
+                                 block_table_tensor=bt.to(DEV), slot_mapping=slots.to(DEV), num_reqs=B,
+                                 num_actual_tokens=B, max_query_len=1)
+    md = builder.build(0, cm)
+    impl = LatentAttentionImpl(24, 256, SCALE, 4)
+
+    class Layer:
+        latent = lat
+    kv_d = kv.to(DEV)
+    output = torch.empty(B, 24, 256, dtype=torch.bfloat16, device=DEV)
+    impl.forward(Layer, q.to(DEV), c.to(DEV), pos.to(DEV), kv_d, md, output)
+    torch.cuda.synchronize()
+    assert bf16_ulp_close(kv_d[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=1)
+    assert_close_out(output, exp, "backend forward")
+    assert impl.forward(Layer, q.to(DEV), c.to(DEV), pos.to(DEV), kv_d, None, output.clone()).abs().sum() == 0
+
+
+def test_decode_long_context_properties():
+    """Config-2 size (B = 64, L = 8192, c50): finite, matches the oracle on a sample of requests, and a request's
+    output does not depend on the others in the batch."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=8193)
+    seqs = [8193] * 64
+    bt, nb, _ = synth.block_tables(seqs, 16)
+    cache = torch.empty(nb, 16, w.layout["row_width"], dtype=torch.bfloat16, device=DEV)
+    synth.fill_cache(cache, w.layout, bt.to(DEV), seqs, seed=21)
+    q = synth.make_queries(64, seed=22).to(DEV)
+    sl = torch.tensor(seqs, dtype=torch.int32, device=DEV)
+    out, *_ = run_decode(lat, q, cache, bt.to(DEV), sl)
+    assert torch.isfinite(out.float()).all()
+    sample = [0, 37, 63]
+    cpu_cache = cache.cpu()
+    exp = oracle.decode_fp32(q[sample].cpu(), cpu_cache, bt[sample], torch.tensor([8193] * 3), ref, SCALE)
+    assert_close_out(out[sample], exp, "config-2 sample")
+    alone, *_ = run_decode(lat, q[37:38], cache, bt[37:38].to(DEV), sl[37:38])
+    err = (alone.float() - out[37:38].float()).abs()
+    assert float(err.max()) < MAX_ABS
