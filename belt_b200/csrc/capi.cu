@@ -273,6 +273,8 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   if (nb_first != n_rope_blocks)
     return fail(BELT_ERR_INVALID, "latent_decode: %d rope blocks given, the groups need %d", n_rope_blocks, nb_first);
   p.n_kst = nk;
+  if (!decode_plan_smem(p))
+    return fail(BELT_ERR_INVALID, "latent_decode: layout (n_k %d, %d rebuild steps) does not fit in shared memory", n_k, nk);
 
   CUtensorMap tm_cache, tm_q;
   {

@@ -34,11 +34,15 @@ struct DecodeParams {
   int kst_group[kDecodeMaxKsteps];
   int kst_first[kDecodeMaxKsteps];
   float scale_log2;
+  // shared-memory layout (byte offsets from the 1024-aligned base), set by the host launcher
+  int stages;
+  int off_q, off_b, off_p, off_red, off_bars, smem_bytes;
 };
 
 cudaError_t launch_latent_decode(const CUtensorMap& tm_cache, const CUtensorMap& tm_q, const DecodeParams& p,
                                  int num_ctas, cudaStream_t stream);
-int decode_smem_bytes();
+// Fills p.stages and the shared-memory offsets; returns false if the layout does not fit.
+bool decode_plan_smem(DecodeParams& p);
 
 // Out[t, g * hpg + j, n] = X[t, g * hpg + j, :] @ W[g, :, n] for n in the group's column runs, 0 elsewhere.
 struct GroupGemmParams {
