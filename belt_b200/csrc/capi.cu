@@ -244,15 +244,36 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   p.num_reqs = num_reqs;
   p.num_blocks = static_cast<int>(num_blocks);
   p.page = page;
-  p.box_rows = page < 128 ? page : 128;
-  p.n_pieces = 128 / p.box_rows;
   p.n_k = n_k;
-  p.n_kp = (n_k + 1) / 2;
   p.v_offset = lk_pad;
   p.r_v = lv;
+  p.n_vc = (lv + 63) / 64;
   p.n_vp = (lv + 127) / 128;
+  // chunked layout: 64-column-aligned parts and whole 64-column chunks inside every row slot
+  const int row_chunks = (row_width + 63) / 64;
+  const bool chunked = lk_pad % 64 == 0 && page % 8 == 0 && static_cast<int64_t>(row_chunks) * 64 <= stride_tok;
+  p.chunked = chunked ? 1 : 0;
+  if (chunked) {
+    p.cps = 4;
+    p.chunk_stride = 1024;
+    p.atom_stride = 4096;
+    p.v_chunk0 = lk_pad / 64;
+  } else {
+    p.cps = 2;
+    p.chunk_stride = 16384;
+    p.atom_stride = 1024;
+    p.v_chunk0 = 0;
+  }
+  p.stage_bytes = p.cps * 128 * 128;
+  p.n_ks = (n_k + p.cps - 1) / p.cps;
+  p.n_vs = (p.n_vc + p.cps - 1) / p.cps;
+  p.box_rows = page < 128 ? page : 128;
+  p.n_pieces = 128 / p.box_rows;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
-  // rebuild K-steps: 16-column steps covering every group's [off, off + rr), read from its rope blocks
+  // rebuild K-steps: 16-column steps covering every group's [off, off + rr), read from its rope blocks; sorted by
+  // column so that the steps of every key pair stage (128 columns) form one range
+  struct Kstep { int col, src, group, first; };
+  Kstep ks_list[kDecodeMaxKsteps];
   int nb_first = 0, nk = 0;
   for (int g = 0; g < kG; ++g) {
     const int off = rope_groups[2 * g], rr = rope_groups[2 * g + 1];
@@ -262,37 +283,90 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
     for (int ks = off / 16; ks <= (off + rr - 1) / 16; ++ks) {
       if (nk >= kDecodeMaxKsteps) return fail(BELT_ERR_INVALID, "latent_decode: too many rebuild K-steps");
       const int col = 16 * ks;
-      p.kst_col[nk] = col;
-      p.kst_src[nk] = (nb_first + (col / 64 - c_lo)) * 64 + col % 64;
-      p.kst_group[nk] = g;
-      p.kst_first[nk] = ks == off / 16;
-      ++nk;
+      ks_list[nk++] = Kstep{col, (nb_first + (col / 64 - c_lo)) * 64 + col % 64, g, ks == off / 16};
     }
     nb_first += c_hi - c_lo + 1;
   }
   if (nb_first != n_rope_blocks)
     return fail(BELT_ERR_INVALID, "latent_decode: %d rope blocks given, the groups need %d", n_rope_blocks, nb_first);
+  for (int i = 1; i < nk; ++i)   // insertion sort by column (stable: a group's steps keep their order)
+    for (int j = i; j > 0 && ks_list[j - 1].col > ks_list[j].col; --j) {
+      const Kstep t = ks_list[j];
+      ks_list[j] = ks_list[j - 1];
+      ks_list[j - 1] = t;
+    }
+  for (int e = 0; e < nk; ++e) {
+    p.kst_col[e] = ks_list[e].col;
+    p.kst_src[e] = ks_list[e].src;
+    p.kst_group[e] = ks_list[e].group;
+    p.kst_first[e] = ks_list[e].first;
+  }
+  for (int k = 0; k < 8; ++k) {
+    p.ks_kst_begin[k] = p.ks_kst_end[k] = 0;
+    if (k >= p.n_ks) continue;
+    const int lo = 64 * p.cps * k, hi = 64 * p.cps * (k + 1);
+    int b = 0;
+    while (b < nk && ks_list[b].col < lo) ++b;
+    int e = b;
+    while (e < nk && ks_list[e].col < hi) ++e;
+    p.ks_kst_begin[k] = b;
+    p.ks_kst_end[k] = e;
+  }
   p.n_kst = nk;
-  if (!decode_plan_smem(p))
+  bool planned = decode_plan_smem(p);
+  if (!planned && chunked) {   // two 64 KB stages do not fit next to this query / rebuild layout: 32 KB page stages
+    p.chunked = 0;
+    p.cps = 2;
+    p.chunk_stride = 16384;
+    p.atom_stride = 1024;
+    p.v_chunk0 = 0;
+    p.stage_bytes = p.cps * 128 * 128;
+    p.n_ks = (n_k + p.cps - 1) / p.cps;
+    p.n_vs = (p.n_vc + p.cps - 1) / p.cps;
+    for (int k = 0; k < 8; ++k) {
+      p.ks_kst_begin[k] = p.ks_kst_end[k] = 0;
+      if (k >= p.n_ks) continue;
+      int b = 0;
+      while (b < nk && ks_list[b].col < 128 * k) ++b;
+      int e = b;
+      while (e < nk && ks_list[e].col < 128 * (k + 1)) ++e;
+      p.ks_kst_begin[k] = b;
+      p.ks_kst_end[k] = e;
+    }
+    planned = decode_plan_smem(p);
+  }
+  if (!planned)
     return fail(BELT_ERR_INVALID, "latent_decode: layout (n_k %d, %d rebuild steps) does not fit in shared memory", n_k, nk);
+  const bool use_chunked = p.chunked != 0;
 
-  CUtensorMap tm_cache, tm_q;
-  {
+  DecodeMaps maps;
+  if (use_chunked) {
+    // {64 columns, page rows, 64-column chunks, blocks}; box {64, 8, n, 1} for n = 1..4 chunks
+    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(page), static_cast<cuuint64_t>(row_chunks),
+                          static_cast<cuuint64_t>(num_blocks)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride_tok) * 2, 128, static_cast<cuuint64_t>(stride_block) * 2};
+    for (int n = 1; n <= 4; ++n) {
+      cuuint32_t box[4] = {64, 8, static_cast<cuuint32_t>(n), 1};
+      int r = encode_bf16(&maps.cache[n - 1], cache, 4, dims, strides, box, "cache");
+      if (r != BELT_OK) return r;
+    }
+  } else {
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_width), static_cast<cuuint64_t>(page),
                           static_cast<cuuint64_t>(num_blocks)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_tok) * 2, static_cast<cuuint64_t>(stride_block) * 2};
     cuuint32_t box[3] = {64, static_cast<cuuint32_t>(p.box_rows), 1};
-    int r = encode_bf16(&tm_cache, cache, 3, dims, strides, box, "cache");
+    int r = encode_bf16(&maps.cache[0], cache, 3, dims, strides, box, "cache");
     if (r != BELT_OK) return r;
+    for (int n = 1; n < 4; ++n) maps.cache[n] = maps.cache[0];
   }
   {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(kq), static_cast<cuuint64_t>(num_reqs) * kH};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(kq) * 2};
     cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kH)};
-    int r = encode_bf16(&tm_q, q_bd, 2, dims, strides, box, "q_bd");
+    int r = encode_bf16(&maps.q, q_bd, 2, dims, strides, box, "q_bd");
     if (r != BELT_OK) return r;
   }
-  cudaError_t e = launch_latent_decode(tm_cache, tm_q, p, num_ctas, as_stream(stream));
+  cudaError_t e = launch_latent_decode(maps, p, num_ctas, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
 }
 

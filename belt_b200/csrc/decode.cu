@@ -5,12 +5,15 @@
 // semantics, 128-token tiles). Twelve warps in three warpgroups; warpgroup 0 gives registers to the other two
 // (setmaxnreg: 80 / 208 / 208 per thread, within the 3 x 168 the launch provides):
 //
-// * warp 0, TMA producer: streams the cache through a ring of 32 KB stages = [128 tokens x 128 features] as two
-//   SWIZZLE_128B halves of [128 x 64]. Pages of 16..128 tokens are fetched as boxes of `page` rows through a 3-D tensor
-//   map over the (possibly strided) [blocks, page, W] cache view; pages past the request are all-OOB boxes (zeros).
-//   Stage order is software-pipelined across tiles: K(0), K(1), V(0), K(2), V(1), ... so that tile i's softmax runs
-//   while tile i+1's key stages are scored and tile i's value stages stream in.
-// * warp 1, tcgen05 issuer (one thread), M = 128 tokens:
+// * warp 0, TMA producer (lanes 0-3 share the boxes of a stage): streams the cache through a ring of stages, each
+//   `cps` 64-column chunks of 128 tokens, all SWIZZLE_128B. Two layouts:
+//     - chunked (64-column-aligned row parts): 4-D boxes of 8 rows x n chunks (one box per 8 tokens, 4 KB for 4
+//       chunks, 512 contiguous bytes per row); a chunk's 8-token atoms sit 4 KB apart. Four lanes issuing 4 KB boxes
+//       keep the HBM near its copy bandwidth, where one lane issuing 2 KB boxes tops out near a third of it;
+//     - page (any 8-aligned layout): 3-D boxes of `page` rows x 64 columns, 2 chunks per stage.
+//   Pages past the request are all-OOB boxes (zeros). Stage order is software-pipelined across tiles: K(0), K(1), V(0),
+//   K(2), V(1), ... so that tile i's softmax runs while tile i+1's key stages are scored and tile i's values stream in.
+// * warp 1, tcgen05 issuer (one thread; descriptors advance only their low words), M = 128 tokens:
 //     - scores S[tok, head] (N = 32: 24 heads; the last 8 columns are ignored) over the K part against the
 //       block-diagonal query;
 //     - the rebuilt RoPE keys gain * B_g c~_g: per group the 16-column K-steps holding its rr_g coordinates against
@@ -20,8 +23,8 @@
 // * warps 2-3: idle.
 // * warps 4-7, rotation: BF16(gain * B_g c~) -> NeoX rotation at each token's position in fp32 -> BF16 operand
 //   (cute_decode.py:473-484), one TMEM lane (token) per thread.
-// * warps 8-11, softmax: masked online softmax in the exp2 domain; the running max of a head is raised only when a tile
-//   exceeds it by more than 2^8 (a warp vote; the O rescale then waits for the previous P.V), P rounded to BF16
+// * warps 8-11, softmax: masked online softmax in the exp2 domain; the running max of a head is raised only when a
+//   tile exceeds it by more than 2^8 (a warp vote; the O rescale then waits for the previous P.V), P rounded to BF16
 //   (cute_decode.py:408); per segment the normalised partial output and its natural-log LSE (cute_decode.py:435-455).
 //
 // TMEM columns: [0, 64) two S buffers, [64, 320) the four groups' rebuilt keys (fp32; the rotated BF16 keys are packed
@@ -37,8 +40,6 @@ namespace belt {
 namespace dec {
 constexpr int kTile = 128;
 constexpr int kMaxStages = 5;
-constexpr int kHalfBytes = kTile * 64 * 2;      // [128 x 64] BF16 = 16 KB
-constexpr int kStageBytes = 2 * kHalfBytes;     // 32 KB
 // A query chunk holds 24 rows of 128 bytes; the score MMA reads 32 rows (N = 32), the last 8 overlapping the next chunk:
 // they only feed S columns 24..31, which nothing reads.
 constexpr int kQChunkBytes = 24 * 128;
@@ -46,6 +47,7 @@ constexpr int kKstBytes = 64 * 16 * 2;          // [64 x 16] BF16 = 2 KB
 constexpr int kPBytes = kTile * 32 * 2;         // [128 tokens x 32 heads] BF16 = 8 KB
 constexpr int kThreads = 384;
 constexpr int kRegsWg0 = 80, kRegsWork = 208;   // 80 + 2 * 208 <= 3 * 168 registers per SMSP
+constexpr int kProducerLanes = 4;
 constexpr int kTmemCols = 512;
 constexpr int kTmemK = 64;
 constexpr int kTmemO = 320;
@@ -77,11 +79,11 @@ bool decode_plan_smem(DecodeParams& p) {
   const int q_bytes = up((p.n_k + kG) * kQChunkBytes + 1024, 1024);
   const int b_bytes = p.n_kst * kKstBytes;
   const int fixed = q_bytes + b_bytes + 2 * kPBytes + up(kRedFloats * 4, 128) + kNumBars * 8 + 16 + 1024;
-  int stages = (kMaxSmem - fixed) / kStageBytes;
+  int stages = (kMaxSmem - fixed) / p.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
   p.stages = stages;
-  p.off_q = stages * kStageBytes;
+  p.off_q = stages * p.stage_bytes;
   p.off_b = p.off_q + q_bytes;
   p.off_p = p.off_b + b_bytes;
   p.off_red = p.off_p + 2 * kPBytes;
@@ -143,6 +145,15 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // Element i (BF16) of 8 x 16 bytes held in registers, as fp32 (i is a compile-time constant after unrolling).
 __device__ __forceinline__ float bf16_lane(const uint4 (&v)[8], int i) {
   const uint4 q = v[i >> 3];
@@ -163,9 +174,9 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+template <bool kChunked>
 __global__ void __launch_bounds__(dec::kThreads, 1)
-    latent_decode_kernel(const __grid_constant__ CUtensorMap tm_cache, const __grid_constant__ CUtensorMap tm_q,
-                         const __grid_constant__ DecodeParams p) {
+    latent_decode_kernel(const __grid_constant__ DecodeMaps maps, const __grid_constant__ DecodeParams p) {
   using namespace dec;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -210,8 +221,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_cache);
-    tma_prefetch_desc(&tm_q);
+    for (int i = 0; i < (kChunked ? 4 : 1); ++i) tma_prefetch_desc(&maps.cache[i]);
+    tma_prefetch_desc(&maps.q);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   if (warp >= 4 && warp < 8 && has_work) {
@@ -236,58 +247,65 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
   if (warp < 4) {
    warpgroup_reg_dealloc<kRegsWg0>();
    if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0 && has_work) {
+    // ------------------------------------------------------------------ TMA producer (lanes 0-3)
+    if (lane < kProducerLanes && has_work) {
       int fills = 0, qsegs = 0;
       bool ok = true;
-      auto acquire = [&](int& st) -> bool {
-        st = fills % S;
+      // the boxes of one stage: chunks [chunk0, chunk0 + nch) of the tile's 128 tokens (chunk = 64 columns from
+      // column `col0`); every lane issues every kProducerLanes-th box, lane 0 arms the barrier first
+      auto load_stage = [&](const TileCursor& c, int col0, int chunk0, int nch) -> bool {
+        const int st = fills % S;
         const int rnd = fills / S;
-        return rnd == 0 || mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
-      };
-      auto tile_blocks = [&](const TileCursor& c, int* blk, int* row) {
+        const bool got =
+            rnd == 0 || mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
+        if (!__all_sync(0xFu, got)) return false;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[bFull + st], nch * kTile * 128);
+        __syncwarp(0xFu);
+        uint8_t* dst = ring + st * p.stage_bytes;
         const int seq = __ldg(p.seq_lens + c.si.b);
         const int npages = (seq + p.page - 1) / p.page;
         const int32_t* bt = p.block_table + static_cast<long long>(c.si.b) * p.bt_stride;
-        for (int pc = 0; pc < p.n_pieces; ++pc) {
-          const int tok0 = c.tile * kTile + pc * p.box_rows;
-          const int pg = tok0 / p.page;
-          row[pc] = tok0 - pg * p.page;
-          blk[pc] = pg < npages ? __ldg(bt + pg) : p.num_blocks;   // past the request: an all-OOB (zero) box
+        if constexpr (kChunked) {
+          for (int b = lane; b < kTile / 8; b += kProducerLanes) {   // 8 tokens per box
+            const int tok0 = c.tile * kTile + 8 * b;
+            const int pg = tok0 / p.page;
+            const int blk = pg < npages ? __ldg(bt + pg) : p.num_blocks;   // past the request: all-OOB (zeros)
+            tma_load_4d(dst + b * p.atom_stride, &maps.cache[nch - 1], &bars[bFull + st], 0, tok0 - pg * p.page,
+                        chunk0, blk);
+          }
+        } else {
+          for (int i = lane; i < nch * p.n_pieces; i += kProducerLanes) {
+            const int h = i / p.n_pieces, pc = i - h * p.n_pieces;
+            const int tok0 = c.tile * kTile + pc * p.box_rows;
+            const int pg = tok0 / p.page;
+            const int blk = pg < npages ? __ldg(bt + pg) : p.num_blocks;
+            tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st],
+                        col0 + 64 * h, tok0 - pg * p.page, blk);
+          }
         }
-      };
-      auto load_stage = [&](int c0, int halves, const int* blk, const int* row) -> bool {
-        int st;
-        if (!acquire(st)) return false;
-        mbar_arrive_expect_tx(&bars[bFull + st], halves * kHalfBytes);
-        uint8_t* dst = ring + st * kStageBytes;
-        for (int h = 0; h < halves; ++h)
-          for (int pc = 0; pc < p.n_pieces; ++pc)
-            tma_load_3d(dst + h * kHalfBytes + pc * p.box_rows * 128, &tm_cache, &bars[bFull + st], c0 + 64 * h,
-                        row[pc], blk[pc]);
         ++fills;
         return true;
       };
       auto load_K = [&](const TileCursor& c) -> bool {
         if (c.first()) {
-          if (qsegs > 0 && !mbar_wait(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer))
-            return false;
-          mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
-          for (int ch = 0; ch < p.n_k + kG; ++ch)
-            tma_load_2d(sQ + ch * kQChunkBytes, &tm_q, &bars[bQFull], ch * 64, c.si.b * kH);
+          const bool got = qsegs == 0 ||
+                           mbar_wait(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
+          if (!__all_sync(0xFu, got)) return false;
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
+            for (int ch = 0; ch < p.n_k + kG; ++ch)
+              tma_load_2d(sQ + ch * kQChunkBytes, &maps.q, &bars[bQFull], ch * 64, c.si.b * kH);
+          }
           ++qsegs;
         }
-        int blk[8], row[8];
-        tile_blocks(c, blk, row);
-        for (int pp = 0; pp < p.n_kp; ++pp)
-          if (!load_stage(128 * pp, (2 * pp + 1 < p.n_k) ? 2 : 1, blk, row)) return false;
+        for (int k = 0; k < p.n_ks; ++k)
+          if (!load_stage(c, 64 * p.cps * k, p.cps * k, min(p.cps, p.n_k - p.cps * k))) return false;
         return true;
       };
       auto load_V = [&](const TileCursor& c) -> bool {
-        int blk[8], row[8];
-        tile_blocks(c, blk, row);
-        for (int j = 0; j < p.n_vp; ++j)
-          if (!load_stage(p.v_offset + 128 * j, (128 * j + 64 < p.r_v) ? 2 : 1, blk, row)) return false;
+        for (int k = 0; k < p.n_vs; ++k)
+          if (!load_stage(c, p.v_offset + 64 * p.cps * k, p.v_chunk0 + p.cps * k, min(p.cps, p.n_vc - p.cps * k)))
+            return false;
         return true;
       };
       TileCursor kc, vc;
@@ -305,14 +323,14 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         if (!(ok = load_V(vc))) break;
         vc.next(p);
       }
-      if (*abort_flag) {
-        // let every copy this thread issued land before the CTA's shared memory goes away
+      if (lane == 0 && *abort_flag) {
+        // let every copy issued land before the CTA's shared memory goes away
         for (int k = max(0, fills - S); k < fills; ++k) mbar_wait_drain(&bars[bFull + k % S], (k / S) & 1);
         if (qsegs > 0) mbar_wait_drain(&bars[bQFull], (qsegs - 1) & 1);
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0 && has_work) {
       constexpr uint32_t idS = idesc_bf16(128, 32, 0, 0);   // scores, K-major A and B
@@ -330,6 +348,17 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         tc_fence_after();
         return true;
       };
+      // Descriptors (16-byte units): every operand's high word is fixed, a K step only moves the low word.
+      const uint32_t hiSw = desc_hi(p.atom_stride, kSwizzle128);     // cache chunks: SBO = 8-token atom stride
+      constexpr uint32_t hiQ = desc_hi(1024, kSwizzle128);          // query chunks: 8 rows = 1 KB
+      constexpr uint32_t hiImg = desc_hi(256, kSwizzleNone);        // rebuild images: 8 rows = 256 B
+      constexpr uint32_t hiP = desc_hi(128, kSwizzleNone);          // P: 8 heads = 128 B
+      const uint32_t loRing = desc_lo(ring_a, 16);                  // + stage, + chunk, + step * 2
+      const uint32_t loRingV = desc_lo(ring_a, p.chunk_stride);     // V^T: LBO = the next 64-feature chunk
+      const uint32_t loQ = desc_lo(q_a, 16);                        // + chunk * 192, + step * 2
+      const uint32_t loImg = desc_lo(b_a, 128);                     // + e * 128
+      const uint32_t loP = desc_lo(p_a, 512);                       // + buffer * 512, + step * 64
+      const uint32_t stage16 = p.stage_bytes >> 4, chunk16 = p.chunk_stride >> 4, pv_step16 = (2 * p.atom_stride) >> 4;
       // key part of tile i: scores into S[i & 1] and the rebuilt RoPE keys
       auto mma_K = [&](const TileCursor& c, int i) -> bool {
         if (c.first()) {
@@ -342,25 +371,23 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         if (i >= 1 && !wait(bSFull + ((i - 1) & 1), ((i - 1) >> 1) & 1)) return false;
         tc_fence_after();
         const uint32_t dS = tmem + 32 * sb;
-        uint32_t acc = 0;
-        for (int pp = 0; pp < p.n_kp; ++pp) {
+        for (int k = 0; k < p.n_ks; ++k) {
           int st;
           if (!full(st)) return false;
-          const uint32_t base = ring_a + st * kStageBytes;
-          for (int i16 = 0; i16 < 8; ++i16) {
-            const int col = 128 * pp + 16 * i16;
-            if (col >= 64 * p.n_k) break;
-            const uint64_t a = smem_desc(base + (i16 >> 2) * kHalfBytes + (i16 & 3) * 32, 16, 1024, kSwizzle128);
-            const uint64_t b = smem_desc(q_a + (col >> 6) * kQChunkBytes + (col & 63) * 2, 16, 1024, kSwizzle128);
-            mma_ss(dS, a, b, idS, acc);
-            acc = 1;
+          const uint32_t a0 = loRing + st * stage16;
+          const int c0 = p.cps * k, c1 = min(p.n_k, c0 + p.cps);
+          for (int cc = c0; cc < c1; ++cc) {
+            const uint32_t ac = a0 + (cc - c0) * chunk16;
+            const uint32_t bq = loQ + cc * (kQChunkBytes >> 4);
+#pragma unroll
+            for (int s16 = 0; s16 < 4; ++s16)
+              mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
           }
-          for (int e = 0; e < p.n_kst; ++e) {
+          for (int e = p.ks_kst_begin[k]; e < p.ks_kst_end[k]; ++e) {
             const int col = p.kst_col[e];
-            if ((col >> 7) != pp) continue;
-            const uint64_t a = smem_desc(base + ((col >> 6) & 1) * kHalfBytes + (col & 63) * 2, 16, 1024, kSwizzle128);
-            const uint64_t b = smem_desc(b_a + e * kKstBytes, 128, 256, kSwizzleNone);
-            mma_ss(tmem + kTmemK + 64 * p.kst_group[e], a, b, idK, p.kst_first[e] ? 0u : 1u);
+            const uint32_t ac = a0 + ((col >> 6) - c0) * chunk16 + ((col & 63) >> 3);
+            mma_ss(tmem + kTmemK + 64 * p.kst_group[e], desc_of(ac, hiSw), desc_of(loImg + e * (kKstBytes >> 4), hiImg),
+                   idK, p.kst_first[e] ? 0u : 1u);
           }
           mma_commit(&bars[bEmpty + st]);
           ++fills;
@@ -373,16 +400,17 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         if (!wait(bKpeFull, i & 1)) return false;
         tc_fence_after();
         const uint32_t dS = tmem + 32 * (i & 1);
+        const uint32_t q0 = loQ + p.n_k * (kQChunkBytes >> 4);
+#pragma unroll
         for (int g = 0; g < kG; ++g)
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t b = smem_desc(q_a + (p.n_k + g) * kQChunkBytes + k * 32, 16, 1024, kSwizzle128);
-            mma_ts(dS, tmem + kTmemK + 64 * g + 8 * k, b, idS, 1u);
-          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_ts(dS, tmem + kTmemK + 64 * g + 8 * k, desc_of(q0 + g * (kQChunkBytes >> 4) + k * 2, hiQ), idS, 1u);
         mma_commit(&bars[bSFull + (i & 1)]);
         if (c.last()) mma_commit(&bars[bQEmpty]);   // the segment's query chunks are read for the last time
         return true;
       };
-      // value part of tile i: O^T += V^T P
+      // value part of tile i: O^T += V^T P, one 128-feature block (two chunks of a stage) at a time
       auto mma_V = [&](const TileCursor& c, int i) -> bool {
         const int pb = i & 1;
         if (!wait(bPFull + pb, (i >> 1) & 1)) return false;
@@ -391,17 +419,21 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
           ++vsegs;
         }
         tc_fence_after();
-        const uint32_t pbase = p_a + pb * kPBytes;
-        for (int j = 0; j < p.n_vp; ++j) {
+        const uint32_t p0 = loP + pb * (kPBytes >> 4);
+        const uint32_t first = c.first() ? 1u : 0u;
+        for (int k = 0; k < p.n_vs; ++k) {
           int st;
           if (!full(st)) return false;
-          const uint32_t base = ring_a + st * kStageBytes;
-          for (int k = 0; k < 8; ++k) {
-            // A = V^T: MN-major SWIZZLE_128B, LBO = the second 64-feature half, SBO = 8 tokens (1 KB)
-            const uint64_t a = smem_desc(base + k * 2048, kHalfBytes, 1024, kSwizzle128);
-            // B = P [tokens x heads]: MN-major no swizzle, LBO = 8 tokens (512 B), SBO = 8 heads (128 B)
-            const uint64_t b = smem_desc(pbase + k * 1024, 512, 128, kSwizzleNone);
-            mma_ss(tmem + kTmemO + 32 * j, a, b, idV, (c.first() && k == 0) ? 0u : 1u);
+          const uint32_t a0 = loRingV + st * stage16;
+          const int j0 = (p.cps * k) >> 1, j1 = min(p.n_vp, (p.cps * (k + 1)) >> 1);
+          for (int j = j0; j < j1; ++j) {
+            const uint32_t aj = a0 + (2 * j - p.cps * k) * chunk16;
+            const uint32_t dO = tmem + kTmemO + 32 * j;
+#pragma unroll
+            for (int s16 = 0; s16 < 8; ++s16)
+              // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
+              mma_ss(dO, desc_of(aj + s16 * pv_step16, hiSw), desc_of(p0 + s16 * (1024 >> 4), hiP), idV,
+                     (first && s16 == 0) ? 0u : 1u);
           }
           mma_commit(&bars[bEmpty + st]);
           ++fills;
@@ -661,18 +693,18 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
 // ---------------------------------------------------------------------------------------------------------------
 // host launch
 // ---------------------------------------------------------------------------------------------------------------
-cudaError_t launch_latent_decode(const CUtensorMap& tm_cache, const CUtensorMap& tm_q, const DecodeParams& p,
-                                 int num_ctas, cudaStream_t stream) {
-  static bool attr_done[64] = {};
+cudaError_t launch_latent_decode(const DecodeMaps& maps, const DecodeParams& p, int num_ctas, cudaStream_t stream) {
+  static bool attr_done[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(latent_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         dec::kMaxSmem);
+  const int m = p.chunked ? 1 : 0;
+  auto kernel = p.chunked ? latent_decode_kernel<true> : latent_decode_kernel<false>;
+  if (dev >= 0 && dev < 64 && !attr_done[m][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kMaxSmem);
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[m][dev] = true;
   }
-  latent_decode_kernel<<<num_ctas, dec::kThreads, p.smem_bytes, stream>>>(tm_cache, tm_q, p);
+  kernel<<<num_ctas, dec::kThreads, p.smem_bytes, stream>>>(maps, p);
   return cudaGetLastError();
 }
 

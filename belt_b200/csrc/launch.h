@@ -26,21 +26,34 @@ struct DecodeParams {
   long long part_ss, part_sh;
   int* err;
   int num_reqs;
-  int num_blocks, page, box_rows, n_pieces;
-  int n_k, n_kp, v_offset, r_v, n_vp;
+  int num_blocks, page;
+  // cache stages: a stage holds `cps` 64-column chunks of 128 tokens. Chunked layout (4-D boxes of 8 rows x nch
+  // chunks): chunks 1 KB apart, 8-token atoms 4 KB apart. Page layout (3-D boxes of box_rows rows x 64 columns): chunks
+  // 16 KB apart, atoms 1 KB apart.
+  int chunked, cps, chunk_stride, atom_stride, stage_bytes;
+  int box_rows, n_pieces;             // page layout: rows per box, boxes per chunk of a tile
+  int n_k, n_ks;                      // key-part chunks and stages
+  int v_offset, v_chunk0, r_v, n_vc, n_vs, n_vp;   // value part: first column (chunk), rank, chunks, stages, O blocks
   int n_kst;
   int kst_col[kDecodeMaxKsteps];
   int kst_src[kDecodeMaxKsteps];
   int kst_group[kDecodeMaxKsteps];
   int kst_first[kDecodeMaxKsteps];
+  int ks_kst_begin[8], ks_kst_end[8];  // rebuild K-steps (sorted by column) inside each key stage
   float scale_log2;
   // shared-memory layout (byte offsets from the 1024-aligned base), set by the host launcher
   int stages;
   int off_q, off_b, off_p, off_red, off_bars, smem_bytes;
 };
 
-cudaError_t launch_latent_decode(const CUtensorMap& tm_cache, const CUtensorMap& tm_q, const DecodeParams& p,
-                                 int num_ctas, cudaStream_t stream);
+// Tensor maps of one decode launch: the cache (page layout: cache[0] only; chunked layout: cache[n - 1] fetches n
+// chunks) and the block-diagonal query.
+struct DecodeMaps {
+  CUtensorMap cache[4];
+  CUtensorMap q;
+};
+
+cudaError_t launch_latent_decode(const DecodeMaps& maps, const DecodeParams& p, int num_ctas, cudaStream_t stream);
 // Fills p.stages and the shared-memory offsets; returns false if the layout does not fit.
 bool decode_plan_smem(DecodeParams& p);
 
