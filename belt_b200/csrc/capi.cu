@@ -67,6 +67,8 @@ cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 }  // namespace
 
+void belt::set_last_error(const char* msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* belt_last_error(void) { return g_last_error.c_str(); }

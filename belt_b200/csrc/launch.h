@@ -109,4 +109,7 @@ struct CacheWriteParams {
 };
 cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 
+// Sets the text belt_last_error() returns on the calling thread.
+void set_last_error(const char* msg);
+
 }  // namespace belt

@@ -4,9 +4,10 @@
  * Every entry point takes plain device pointers, element strides and sizes, launches on the given CUDA stream
  * (a cudaStream_t passed as void*, NULL = the legacy default stream), allocates nothing and returns
  * BELT_OK or a negative status; belt_last_error() then describes the failure (thread-local). Launches are
- * asynchronous; they can be captured in CUDA graphs. BF16 tensors are passed as `const void*` / `void*`.
+ * asynchronous. The launches of the entry points that take every buffer from the caller can be captured in CUDA
+ * graphs. BF16 tensors are passed as `const void*` / `void*`.
  *
- * Each entry point replaces one operator of the reference's vLLM plugin
+ * Each entry point but belt_latent_decode_noalloc replaces one operator of the reference's vLLM plugin
  * (liuyaoyang04/BELT, plugins/vllm_lrkv/vllm_lrkv/), cited per function.
  */
 #ifndef BELT_B200_H_
@@ -109,6 +110,30 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
 int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
                         int32_t num_reqs, int32_t nh, int32_t lv, void* out, int64_t out_sb, int64_t out_sh,
                         float* lse, int64_t lse_sb, void* stream);
+
+/*
+ * One decode step of a compressed layer with no caller-provided scratch: belt_decode_schedule, belt_latent_decode
+ * and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
+ * 24 MiB array inside this library instead of buffers from the caller. It has no counterpart in the reference
+ * (whose decode allocates its partials per call); it exists for callers that cannot allocate device memory: hosts
+ * binding this ABI that hold only the engine's KV pool, query and output buffers, and engines that reserved nearly
+ * all of HBM for the KV pool at start-up. It calls no allocating routine.
+ *   Arguments as belt_latent_decode, minus work / cta_seg / part, plus min_tiles (belt_decode_schedule) and the
+ *   merged outputs out [num_reqs, 24, lv] BF16 (strides out_sb, out_sh) and lse [num_reqs, 24] fp32 (row stride
+ *   lse_sb), as belt_merge_segments. Pointers and `stream` belong to the current device.
+ *   Limits (BELT_ERR_INVALID beyond them, before anything runs): num_reqs <= 4096, num_ctas <= 1024, and
+ *   (num_reqs + num_ctas) * 24 * (lv + 1) * 4 bytes <= 24 MiB - 128 KiB (lv = 640, 148 CTAs: 259 requests).
+ *   The first call on a device looks up the array's device address (cudaGetSymbolAddress) for that device; make it
+ *   before any stream capture begins. All calls on a device share the array and leave their contents in it; calls
+ *   that overlap on the GPU (unordered streams or host threads of one device) race on it.
+ */
+int belt_latent_decode_noalloc(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                               int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                               const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                               int32_t num_ctas, int32_t min_tiles, float sm_scale, int32_t lk_pad, int32_t lv,
+                               const int32_t* rope_groups, const void* rope_blocks, int32_t n_rope_blocks,
+                               const void* cos_sin, int32_t max_pos, void* out, int64_t out_sb, int64_t out_sh,
+                               float* lse, int64_t lse_sb, int32_t* err, void* stream);
 
 /* Number of SMs of `device` (the decode grid: one CTA per SM). */
 int belt_num_sms(int32_t device);
