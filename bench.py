@@ -184,54 +184,100 @@ class Workload:
 
 # ------------------------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
+    """SM clock, power and clock-event reasons of this rank's GPU, sampled every 10 ms by a thread reading NVML while
+    the timed region runs (``nvidia-smi -lms 200`` as the fallback when NVML is unavailable)."""
+
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.samples = []            # (sm MHz, max sm MHz, power W, {reason names})
+        self.thread = self.proc = self.path = None
+        self.stop_flag = False
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+        for cand in (uuid, "GPU-" + uuid):
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(cand)
+            except pynvml.NVMLError:
+                pass
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+
+    def _poll(self, nv, h):
+        bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+        smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop_flag:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), float(smax), pw, {n for n, b in bits.items() if r & b}))
+            except nv.NVMLError:
+                pass
+            time.sleep(0.01)
 
     def start(self):
         try:
+            import threading
+            nv, h = self._nvml_handle()
+            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.thread.start()
+            self.source = "nvml 10 ms"
+            return
+        except Exception:  # NVML missing or refused: fall back to nvidia-smi
+            self.thread = None
+        try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device.index or 0), f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi 200 ms"
         except (OSError, FileNotFoundError):
             self.proc = None
 
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    def _read_smi(self):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, smax, reasons, power = [], [], set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-                power.append(float(f[3]))
+                self.samples.append((float(f[1]), float(f[2]), float(f[3]),
+                                     {n for n, v in zip(self.REASONS, f[5:9]) if v.lower() == "active"}))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
         os.unlink(self.path)
-        if not sm:
+
+    def stop(self) -> dict:
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+        elif self.proc is not None:
+            self._read_smi()
+        else:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [s for s, p in zip(sm, power) if p > 0.3 * max(power)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm), "power_w_max": max(power)}
+        power = [s[2] for s in self.samples]
+        loaded = [s for s in self.samples if s[2] > 0.3 * max(power)] or self.samples
+        reasons = sorted(set().union(*(s[3] for s in self.samples)))
+        return {"sm_mhz": statistics.median(s[0] for s in loaded), "sm_max_mhz": max(s[1] for s in self.samples),
+                "reasons": reasons, "samples": len(self.samples), "power_w_max": max(power), "source": self.source}
 
 
 # ------------------------------------------------------------------------------------------------------------ CPU arm
@@ -386,7 +432,7 @@ def main():
 
     dec_events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(wl.L)] for _ in range(args.steps)]
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
     barrier(dist)
     clocks.start()
     time.sleep(0.3)
@@ -435,7 +481,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "peak_source": peak_src,
                          "kernel": "latent_decode_kernel", "kernel_ms_per_launch": sum(kern_ms) / wl.L,
-                         "traffic": traffic_per_launch / wl.L if traffic_per_launch else None},
+                         "traffic": traffic_per_launch, "traffic_source": traffic and traffic.get("source")},
             "clocks": clk,
             "gpu_launches": wl.launches_per_step * args.steps}
     if not args.no_e2e:
