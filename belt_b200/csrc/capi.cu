@@ -65,6 +65,64 @@ int encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* 
 
 cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Out = X W per head's group (block_diag_query, up_project): on the tensor cores when TMA can describe X and W
+// (16-byte aligned bases and strides, W rows contiguous), else on the SIMT kernel.
+int run_group_product(const belt::GroupGemmParams& gp, const char* what, cudaStream_t stream) {
+  const bool tma_ok = aligned16(gp.X) && aligned16(gp.W) && gp.swn == 1 && gp.sxh > 0 && gp.sxt > 0 &&
+                      (gp.sxh * 2) % 16 == 0 && (gp.sxt * 2) % 16 == 0 && (gp.swk * 2) % 16 == 0 &&
+                      (gp.swg * 2) % 16 == 0 && gp.K > 0 && gp.sxh >= gp.K &&
+                      gp.sxt >= static_cast<long long>(gp.G * gp.hpg) * gp.sxh && gp.swk >= gp.N &&
+                      gp.swg >= static_cast<long long>(gp.K) * gp.swk;
+  cudaError_t e;
+  if (tma_ok) {
+    belt::HeadGemmMaps maps;
+    {
+      cuuint64_t dims[3] = {static_cast<cuuint64_t>(gp.K), static_cast<cuuint64_t>(gp.G * gp.hpg),
+                            static_cast<cuuint64_t>(gp.T)};
+      cuuint64_t strides[2] = {static_cast<cuuint64_t>(gp.sxh) * 2, static_cast<cuuint64_t>(gp.sxt) * 2};
+      cuuint32_t box[3] = {64, 1, 128};
+      int r = encode_bf16(&maps.x, gp.X, 3, dims, strides, box, what);
+      if (r != BELT_OK) return r;
+    }
+    {
+      cuuint64_t dims[3] = {static_cast<cuuint64_t>(gp.N), static_cast<cuuint64_t>(gp.K),
+                            static_cast<cuuint64_t>(gp.G)};
+      cuuint64_t strides[2] = {static_cast<cuuint64_t>(gp.swk) * 2, static_cast<cuuint64_t>(gp.swg) * 2};
+      cuuint32_t box[3] = {64, 64, 1};
+      int r = encode_bf16(&maps.w, gp.W, 3, dims, strides, box, what);
+      if (r != BELT_OK) return r;
+    }
+    belt::HeadGemmParams hp{};
+    hp.Out = gp.Out;
+    hp.sot = gp.sot;
+    hp.soh = gp.soh;
+    hp.T = gp.T;
+    hp.K = gp.K;
+    hp.N = gp.N;
+    hp.hpg = gp.hpg;
+    hp.G = gp.G;
+    for (int g = 0; g < 4; ++g) {
+      hp.nruns[g] = gp.nruns[g];
+      for (int i = 0; i < 3; ++i) {
+        hp.run_lo[g][i] = gp.run_lo[g][i];
+        hp.run_hi[g][i] = gp.run_hi[g][i];
+      }
+    }
+    hp.nb = 2;
+    hp.vec_out = aligned16(gp.Out) && gp.sot % 8 == 0 && gp.soh % 8 == 0;
+    hp.err = nullptr;
+    e = belt::launch_head_gemm(maps, hp, stream);
+  } else {
+    e = belt::launch_group_gemm(gp, stream);
+  }
+  if (e != cudaSuccess) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "%s launch", what);
+    return cuda_fail(e, buf);
+  }
+  return BELT_OK;
+}
+
 }  // namespace
 
 void belt::set_last_error(const char* msg) { g_last_error = msg; }
@@ -126,8 +184,8 @@ int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64
       p.run_hi[g][i] = hi;
     }
   }
-  cudaError_t e = belt::launch_group_gemm(p, as_stream(stream));
-  return e == cudaSuccess ? ok() : cuda_fail(e, "block_diag_query launch");
+  const int r = run_group_product(p, "block_diag_query", as_stream(stream));
+  return r == BELT_OK ? ok() : r;
 }
 
 int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_sh, int32_t r_v, const void* v_up_t,
@@ -156,8 +214,8 @@ int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_s
     p.run_lo[g][0] = 0;
     p.run_hi[g][0] = belt::kD;
   }
-  cudaError_t e = belt::launch_group_gemm(p, as_stream(stream));
-  return e == cudaSuccess ? ok() : cuda_fail(e, "up_project launch");
+  const int r = run_group_product(p, "up_project", as_stream(stream));
+  return r == BELT_OK ? ok() : r;
 }
 
 int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, const void* slots, int32_t slots_i64,

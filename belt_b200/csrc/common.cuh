@@ -99,6 +99,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait that no abort flag cuts short (for waits that must see in-flight work finish, e.g. before freeing
+// TMEM). Records `code` in *err (if given) and returns false after `limit` cycles.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                  long long limit = kWaitCycles) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_sleep(bar, parity, 100000)) {
+    if (clock64() - t0 > limit) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // TMA (tensor maps live in kernel parameter space; no multicast anywhere)
 // ---------------------------------------------------------------------------------------------------------------

@@ -71,6 +71,26 @@ struct GroupGemmParams {
 };
 cudaError_t launch_group_gemm(const GroupGemmParams& p, cudaStream_t stream);
 
+// The same product on the tensor cores (head_gemm.cu): X and W through TMA maps, Out written directly.
+//   maps.x: 3-D {K, heads, T} over X (strides sxh, sxt), box {64, 1, 128};
+//   maps.w: 3-D {N, K, G} over W (strides swk, swg; swn = 1), box {64, 64, 1}.
+struct HeadGemmMaps {
+  CUtensorMap x;
+  CUtensorMap w;
+};
+struct HeadGemmParams {
+  __nv_bfloat16* Out;
+  long long sot, soh;
+  int T, K, N, hpg, G;
+  int nruns[4];
+  int run_lo[4][3], run_hi[4][3];
+  int nb;        // column tile = 64 * nb (1, 2 or 4)
+  int vec_out;   // Out rows 16-byte aligned: 16-byte stores
+  int stages;    // set by the launcher
+  int* err;
+};
+cudaError_t launch_head_gemm(const HeadGemmMaps& maps, HeadGemmParams p, cudaStream_t stream);
+
 struct ScheduleParams {
   const int32_t* seq_lens;
   int num_reqs, num_ctas, min_tiles, tile;
