@@ -21,6 +21,8 @@ SIGNATURES = {
     "belt_up_project": [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp],
     "belt_latent_rows_to_cache": [c_vp, c_i64, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp,
                                   c_i32, c_i32p, c_f32, c_vp],
+    "belt_latent_proj_rows_to_cache": [c_vp, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32,
+                                       c_i64, c_i64, c_vp, c_i32, c_i32p, c_f32, c_vp, c_vp],
     "belt_latent_decode": [c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp,
                            c_vp, c_i32, c_vp, c_i64, c_i64, c_f32, c_i32, c_i32, c_i32p, c_vp, c_i32, c_vp, c_i32,
                            c_vp, c_vp],

@@ -256,6 +256,103 @@ int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, c
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
 }
 
+int belt_latent_proj_rows_to_cache(const void* x, int64_t num_tokens, int64_t x_st, int32_t hidden,
+                                   const void* w_down, int64_t w_st, const void* slots, int32_t slots_i64,
+                                   void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                                   int64_t stride_block, int64_t stride_tok, const void* u_cat, int32_t lk,
+                                   const int32_t* k_segs, float eps, int32_t* err, void* stream) {
+  if (num_tokens < 0 || page <= 0 || row_width <= 0 || lk <= 0 || lk > row_width || !k_segs || num_blocks < 0 ||
+      hidden <= 0)
+    return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: bad arguments");
+  if (num_tokens == 0) return ok();
+  if (!x || !w_down || !slots || !cache || !u_cat) return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: null buffer");
+  if (hidden % 8 || x_st < hidden || x_st % 8 || w_st < hidden || w_st % 8 || !aligned16(x) || !aligned16(w_down) ||
+      !aligned16(u_cat))
+    return fail(BELT_ERR_INVALID,
+                "latent_proj_rows_to_cache: x and W_down need 16-byte aligned rows (hidden %d, strides %lld, %lld)",
+                hidden, (long long)x_st, (long long)w_st);
+  if (stride_tok < row_width) return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: token stride < row width");
+  if (num_tokens > (1ll << 31) - 1) return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: too many tokens");
+  belt::ProjWriteParams p{};
+  p.slots = slots;
+  p.slots_i64 = slots_i64 ? 1 : 0;
+  p.num_slots = num_blocks * page;
+  p.cache = static_cast<__nv_bfloat16*>(cache);
+  p.sblk = stride_block;
+  p.stok = stride_tok;
+  p.page = page;
+  p.W = row_width;
+  p.lk = lk;
+  p.T = static_cast<int>(num_tokens);
+  p.hidden = hidden;
+  p.G = belt::kG;
+  p.eps = eps;
+  p.vec_ok = aligned16(cache) && stride_tok % 8 == 0 && stride_block % 8 == 0;
+  p.err = err;
+  // work items: every group's 64-column window, then the V part [lk, W) in windows of four chunks
+  int items = 0;
+  for (int g = 0; g < belt::kG; ++g) {
+    p.a_lo[g] = k_segs[4 * g];
+    p.a_n[g] = k_segs[4 * g + 1];
+    p.b_lo[g] = k_segs[4 * g + 2];
+    p.b_n[g] = k_segs[4 * g + 3];
+    const int r = p.a_n[g] + p.b_n[g];
+    if (p.a_lo[g] < 0 || p.b_lo[g] < 0 || p.a_n[g] < 0 || p.b_n[g] < 0 || r > 256 ||
+        p.a_lo[g] + p.a_n[g] > lk || (p.b_n[g] > 0 && p.b_lo[g] + p.b_n[g] > lk))
+      return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: k_segs of group %d out of range (lk %d)", g, lk);
+    bool use[64] = {};
+    const int runs[2][2] = {{p.a_lo[g], p.a_n[g]}, {p.b_lo[g], p.b_n[g]}};
+    for (int q = 0; q < 2; ++q)
+      if (runs[q][1] > 0)
+        for (int c = runs[q][0] >> 6; c <= (runs[q][0] + runs[q][1] - 1) >> 6 && c < 64; ++c) use[c] = true;
+    int n = 0;
+    for (int c = 0; c < 64; ++c)
+      if (use[c]) {
+        if (n == belt::kPwMaxChunks)
+          return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: group %d spans more than %d 64-column chunks", g,
+                      belt::kPwMaxChunks);
+        p.item_chunk[items][n++] = c;
+      }
+    if (n == 0) {   // a group without coordinates still gets an item (nothing to write); keep one chunk to stream
+      p.item_chunk[items][0] = 0;
+      n = 1;
+    }
+    p.item_nch[items++] = n;
+  }
+  for (int c = lk >> 6; c < (row_width + 63) >> 6; c += 4) {
+    if (items == belt::kPwMaxItems)
+      return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: V part too wide (%d columns)", row_width - lk);
+    const int n = ((row_width + 63) >> 6) - c < 4 ? ((row_width + 63) >> 6) - c : 4;
+    for (int i = 0; i < n; ++i) p.item_chunk[items][i] = c + i;
+    p.item_nch[items++] = n;
+  }
+  p.n_items = items;
+  belt::ProjWriteMaps maps;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(num_tokens)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(x_st) * 2};
+    cuuint32_t box[2] = {64, 128};
+    int r = encode_bf16(&maps.x, x, 2, dims, strides, box, "x");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(row_width)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(w_st) * 2};
+    cuuint32_t box[2] = {64, 64};
+    int r = encode_bf16(&maps.w, w_down, 2, dims, strides, box, "w_down");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(belt::kG * belt::kD), static_cast<cuuint64_t>(lk)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(belt::kG * belt::kD) * 2};
+    cuuint32_t box[2] = {64, 64};
+    int r = encode_bf16(&maps.u, u_cat, 2, dims, strides, box, "u_cat");
+    if (r != BELT_OK) return r;
+  }
+  cudaError_t e = belt::launch_proj_write(maps, p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "latent_proj_rows_to_cache launch");
+}
+
 int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
                        int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
                        const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* work,

@@ -129,6 +129,35 @@ struct CacheWriteParams {
 };
 cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 
+// Fused latent cache write (proj_write.cu): c = bf16(x W_down^T), the RMS fold of every K group, paged scatter.
+//   maps.x: 2-D {hidden, T} over x, box {64, 128}; maps.w: 2-D {hidden, W} over W_down, box {64, 64};
+//   maps.u: 2-D {G * 256, lk} over u_cat, box {64, 64}.
+// Work items: KV groups 0..G-1, then chunks of the V part [lk, W); item i covers the 64-column chunks
+// item_chunk[i][0 .. item_nch[i]) of the row (ascending).
+constexpr int kPwMaxChunks = 5;
+constexpr int kPwMaxItems = 12;
+struct ProjWriteMaps {
+  CUtensorMap x;
+  CUtensorMap w;
+  CUtensorMap u;
+};
+struct ProjWriteParams {
+  const void* slots;
+  int slots_i64;
+  long long num_slots;
+  __nv_bfloat16* cache;
+  long long sblk, stok;
+  int page, W, lk, T, hidden, G;
+  int a_lo[4], a_n[4], b_lo[4], b_n[4];
+  int n_items;
+  int item_nch[kPwMaxItems];
+  int item_chunk[kPwMaxItems][kPwMaxChunks];
+  float eps;
+  int vec_ok;   // cache rows 16-byte aligned
+  int* err;
+};
+cudaError_t launch_proj_write(const ProjWriteMaps& maps, const ProjWriteParams& p, cudaStream_t stream);
+
 // Sets the text belt_last_error() returns on the calling thread.
 void set_last_error(const char* msg);
 

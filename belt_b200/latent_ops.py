@@ -6,7 +6,9 @@
 * ``up_project``: the merged latent output [T, H, r_v] times U_v of each head's group (stored transposed as
   [G, r_v, D]) -> the attention output [T, H, D], in place (latent_ops.py:76-81);
 * ``latent_rows_to_cache``: the per-token cache rows ``[c_K / rho | 0 | c_v | 0]`` into the paged KV cache
-  (latent_ops.py:138-158).
+  (latent_ops.py:138-158);
+* ``project_rows_to_cache``: the same rows computed from the layer inputs, the model's ``kv_latent_proj`` linear
+  (models/qwen3_5_latent.py:139-140, 213) fused into the write on the tensor cores.
 """
 
 from __future__ import annotations
@@ -103,3 +105,30 @@ def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: tor
               int(slot_mapping.dtype == torch.int64), cache.data_ptr(), cache.shape[0], cache.shape[1], W,
               cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk, _lib.int_array(segs), float(eps),
               _stream_ptr(c.device))
+
+
+def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor,
+                          u_cat: torch.Tensor, k_segs, eps: float) -> None:
+    """``latent_rows_to_cache(bf16(x @ w_down^T), ...)`` in one kernel: x [T, hidden] BF16 (the layer inputs of the new
+    tokens), w_down [>= W, hidden] BF16 (``kv_latent_proj.weight``, zero rows at the gaps), the other arguments as
+    ``latent_rows_to_cache``. The latent projection itself is never materialised."""
+    T = slot_mapping.shape[0]
+    if T == 0:
+        return
+    lk, ngd = u_cat.shape
+    segs = host_k_segs(k_segs)
+    if len(segs) != 16 or ngd != 4 * HEAD_DIM:
+        raise ValueError("project_rows_to_cache: head dim 256, 4 groups, k_segs [4, 4]")
+    W = cache.shape[-1]
+    for name, t in (("x", x), ("w_down", w_down), ("cache", cache), ("u_cat", u_cat)):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError(f"project_rows_to_cache: {name} must be BF16 with contiguous rows")
+    if x.shape[0] < T or w_down.shape[0] < W or w_down.shape[1] != x.shape[1] or not u_cat.is_contiguous():
+        raise ValueError("project_rows_to_cache: x [T, hidden], w_down [>= W, hidden], contiguous u_cat")
+    if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous():
+        raise ValueError("project_rows_to_cache: contiguous int32 / int64 slot_mapping")
+    from .decode import error_word
+    _lib.call("belt_latent_proj_rows_to_cache", x.data_ptr(), T, x.stride(0), x.shape[1], w_down.data_ptr(),
+              w_down.stride(0), slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), cache.data_ptr(),
+              cache.shape[0], cache.shape[1], W, cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk,
+              _lib.int_array(segs), float(eps), error_word(x.device).data_ptr(), _stream_ptr(x.device))

@@ -77,6 +77,22 @@ int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, c
                               void* stream);
 
 /*
+ * Fused latent cache write with the down-projection: replaces the model's `kv_latent_proj` linear
+ * (models/qwen3_5_latent.py:139-140, 213; weight rows laid out by lrkv/runtime/export_latent.py:193-205) followed by
+ * latent_ops.py:138-158 (`latent_rows_to_cache`). x [T, hidden] BF16 (row stride x_st) are the layer's inputs of the
+ * new tokens; w_down [>= row_width, hidden] BF16 (row stride w_st) is `kv_latent_proj.weight` (zero rows at the gaps).
+ * c = bf16(x w_down^T) is never stored: the kernel writes rows [c_K / rho | c[lk:W]] at slots as
+ * belt_latent_rows_to_cache does with that c. hidden, x_st and w_st multiples of 8, x / w_down / u_cat 16-byte
+ * aligned. Every group's runs must fit in five 64-column chunks (always true for ranks <= 256). err: optional device
+ * word for a wait that timed out.
+ */
+int belt_latent_proj_rows_to_cache(const void* x, int64_t num_tokens, int64_t x_st, int32_t hidden,
+                                   const void* w_down, int64_t w_st, const void* slots, int32_t slots_i64,
+                                   void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                                   int64_t stride_block, int64_t stride_tok, const void* u_cat, int32_t lk,
+                                   const int32_t* k_segs, float eps, int32_t* err, void* stream);
+
+/*
  * Single-pass paged latent decode (split-KV partials): replaces cute_decode.py:649-678 (`latent_decode_cute`,
  * kernel `LatentDecodeSm90` :90-484).
  *   q_bd [num_reqs, 24, kq] BF16 contiguous (belt_block_diag_query), kq = n_k * 64 + 4 * 64, n_k = ceil(lk_pad / 64);

@@ -28,7 +28,7 @@ ALIGN = 8
 
 __all__ = [
     "H", "G", "D", "ROT", "CHUNK", "HPG", "ALIGN", "align", "k_segments", "row_layout", "rope_basis",
-    "build_latent_layer", "rope_cos_sin", "derive", "rope_blocks", "latent_rows", "block_diag_query",
+    "build_latent_layer", "rope_cos_sin", "derive", "rope_blocks", "latent_rows", "project_rows", "block_diag_query",
     "block_diag_query_construct", "up_project", "decompress", "attend", "gather_rows", "decode_reference",
     "decode_fp32", "schedule", "decode_partials", "merge_segments", "decode_kernel_path",
 ]
@@ -185,6 +185,15 @@ def latent_rows(c, slot_mapping, cache, u_cat, k_segs, eps):
             inv = torch.rsqrt((k_pre * k_pre).sum() / Dh + eps)
             row[cols] = (cf[t, cols] * inv).to(cache.dtype)
     return cache
+
+
+def project_rows(x, w_down, slot_mapping, cache, u_cat, k_segs, eps):
+    """The model's down-projection followed by the cache write: c = bf16(x @ w_down^T) (``kv_latent_proj``,
+    ``qwen3_5_latent.py:139-140, 213``: a BF16 linear with FP32 accumulation), then ``latent_rows``
+    (``latent_ops.py:85-158``)."""
+    W = cache.shape[2]
+    c = (x.float() @ w_down[:W].float().t()).to(torch.bfloat16)
+    return latent_rows(c, slot_mapping, cache, u_cat, k_segs, eps)
 
 
 def block_diag_query(q, qmap):

@@ -54,8 +54,8 @@ class UlpCheck:
         return f"UlpCheck({self.ok}: {self.msg})"
 
 
-def bf16_ulp_close(a, b, ulps=1):
-    """|a - b| <= ulps BF16 ulps of max(|a|, |b|) elementwise (NaN positions must agree)."""
+def bf16_ulp_close(a, b, ulps=1, atol=0.0):
+    """|a - b| <= ulps BF16 ulps of max(|a|, |b|) + atol elementwise (NaN positions must agree)."""
     a, b = a.float(), b.float()
     na, nb = torch.isnan(a), torch.isnan(b)
     if not torch.equal(na, nb):
@@ -65,7 +65,7 @@ def bf16_ulp_close(a, b, ulps=1):
     a, b = a[m], b[m]
     mag = torch.maximum(a.abs(), b.abs())
     ulp = torch.where(mag > 0, 2.0 ** (torch.floor(torch.log2(mag.clamp_min(1e-38))) - 7), torch.zeros_like(mag))
-    bad = (a - b).abs() > ulps * ulp + 1e-30
+    bad = (a - b).abs() > ulps * ulp + atol + 1e-30
     if bad.any():
         r = ((a - b).abs() / ulp.clamp_min(1e-38))[bad]
         i = bad.nonzero()[:3].flatten().tolist()

@@ -127,6 +127,92 @@ def test_cache_write_strided_view_and_padding():
     assert not full[:, 0].any() and not full[:, 2].any()          # neighbouring layers untouched
 
 
+# ------------------------------------------------------------------------------------------------- fused down-projection
+# The kernel rounds c = x W_down^T to BF16 after an FP32 sum over `hidden` terms in another order than the oracle's
+# (the reference's own cuBLAS linear has the same freedom). An element of c can then sit one BF16 ulp away, and the
+# folded value c * inv at most 2 ulps; near zero the sum's own error, ~sqrt(hidden) * 2^-24 * sum|x w| (~1e-5 for
+# hidden = 1024 and unit-scale rows), dominates the ulp, hence the absolute floor PROJ_ATOL. Placement stays bit-exact.
+PROJ_ATOL = 2e-5
+
+
+@pytest.mark.parametrize("name", CASES)
+@pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
+def test_proj_write(name, slot_dtype):
+    fx, spec, w, batch, q = golden_case(name)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    page, nb = fx["page"], fx["cw_nb"]
+    slots = fx["cw_slots"]
+    T = slots.shape[0]
+    x = torch.randn(T, spec.hidden, generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
+    init = torch.full((nb, page, W), float("nan")).to(torch.bfloat16)
+    init.view(-1, W)[::3] = 1.5
+    exp = oracle.project_rows(x, w.kv_latent_proj, slots, init.clone(), ref["u_cat"], ref["k_segs"], 1e-6)
+    cache = init.clone().to(DEV)
+    latent_ops.project_rows_to_cache(x.to(DEV), w.kv_latent_proj.to(DEV), slots.to(slot_dtype).to(DEV), cache,
+                                     lat.u_cat, lat.k_segs, 1e-6)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    got = cache.cpu()
+    written = slots[slots >= 0].long()
+    untouched = torch.ones(nb * page, dtype=torch.bool)
+    untouched[written] = False
+    assert torch.equal(got.view(-1, W)[untouched].view(torch.int16), init.view(-1, W)[untouched].view(torch.int16))
+    assert bf16_ulp_close(got.view(-1, W)[written], exp.view(-1, W)[written], ulps=2, atol=PROJ_ATOL)
+
+
+def test_proj_write_strided_view_multi_tile():
+    """300 tokens (three 128-token tiles, the last one ragged), padding slots, the middle layer of a block-outermost
+    buffer: neighbouring layers stay zero."""
+    spec = synth.spec_from_ranks(448, 576)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    page, nb, layers = 16, 40, 3
+    buf = torch.zeros(nb, layers, page, W, dtype=torch.bfloat16, device=DEV)
+    view = buf[:, 1]
+    T = 300
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
+    slots = torch.randperm(nb * page, generator=g)[:T]
+    slots[::7] = -1
+    latent_ops.project_rows_to_cache(x.to(DEV), w.kv_latent_proj.to(DEV), slots.to(DEV), view, lat.u_cat,
+                                     lat.k_segs, 1e-6)
+    exp = oracle.project_rows(x, w.kv_latent_proj, slots, torch.zeros(nb, page, W, dtype=torch.bfloat16),
+                              ref["u_cat"], ref["k_segs"], 1e-6)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    full = buf.cpu()
+    assert bf16_ulp_close(full[:, 1], exp, ulps=2, atol=PROJ_ATOL)
+    assert not full[:, 0].any() and not full[:, 2].any()
+
+
+def test_proj_write_prefill_chunk():
+    """An 8192-token chunk (the chunked-prefill write), checked on a sample of 256 tokens against the oracle."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    T, page = 8192, 16
+    nb = T // page + 8
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(T, spec.hidden, generator=g).to(torch.bfloat16)
+    slots = torch.randperm(nb * page, generator=g)[:T]
+    cache = torch.zeros(nb, page, W, dtype=torch.bfloat16, device=DEV)
+    latent_ops.project_rows_to_cache(x.to(DEV), w.kv_latent_proj.to(DEV), slots.to(DEV), cache, lat.u_cat,
+                                     lat.k_segs, 1e-6)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    sample = torch.randperm(T, generator=g)[:256]
+    exp = oracle.project_rows(x[sample], w.kv_latent_proj, slots[sample], torch.zeros(nb, page, W,
+                              dtype=torch.bfloat16), ref["u_cat"], ref["k_segs"], 1e-6)
+    got = cache.cpu().view(-1, W)[slots[sample]]
+    assert bf16_ulp_close(got, exp.view(-1, W)[slots[sample]], ulps=2, atol=PROJ_ATOL)
+    written = torch.zeros(nb * page, dtype=torch.bool)
+    written[slots] = True
+    assert not cache.cpu().view(-1, W)[~written].any()
+
+
 # ------------------------------------------------------------------------------------------------- query / up-projection
 @pytest.mark.parametrize("name", CASES)
 def test_block_diag_query(name):
