@@ -271,6 +271,23 @@ class LatentAttentionImpl:
             tok += ql
 
 
+def latent_attention_step(impl: "LatentAttentionImpl", layer, query: torch.Tensor, hidden: torch.Tensor,
+                          w_down: torch.Tensor, kv_cache: torch.Tensor, attn_metadata: LatentAttentionMetadata,
+                          output: torch.Tensor) -> torch.Tensor:
+    """The attention half of one compressed layer as the model runs it (models/qwen3_5_latent.py:204-217:
+    ``key = kv_latent_proj(hidden)``, then the backend's cache write and attention), with the down-projection fused
+    into the cache write: the rows of every scheduled token (``attn_metadata.slot_mapping``) are computed from
+    ``hidden`` [T, hidden_size] and ``w_down`` (``kv_latent_proj.weight`` [>= row_width, hidden_size]) and written in
+    one kernel, then ``impl.forward`` attends with ``key=None`` (nothing left to write)."""
+    if attn_metadata is None:
+        return output.fill_(0)
+    lat: LatentLayer = layer.latent
+    if attn_metadata.slot_mapping is not None:
+        latent_ops.project_rows_to_cache(hidden, w_down, attn_metadata.slot_mapping, kv_cache[:, 0], lat.u_cat,
+                                         lat.k_segs_host, lat.eps)
+    return impl.forward(layer, query, None, None, kv_cache, attn_metadata, output)
+
+
 class LatentAttentionBackend:
     # the op writes the rows itself; False keeps vLLM padding the slot mapping to the token count of the key
     forward_includes_kv_cache_update: bool = False

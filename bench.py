@@ -130,9 +130,12 @@ class Workload:
         self.caches = [self.buf[:, l] for l in range(self.L)]
         gq = torch.Generator(device=device).manual_seed(synth.SEED_QUERY + rank)
         self.q = torch.randn(self.L, self.B, H, D, generator=gq, device=device, dtype=torch.bfloat16)
-        self.c = torch.randn(self.L, self.B, W, generator=gq, device=device, dtype=torch.bfloat16)
-        for l, w in enumerate(self.weights):
-            self.c[l] *= synth.latent_columns(w.layout).to(device)
+        hiddens = {s.hidden for s in specs}
+        assert len(hiddens) == 1, "one hidden size per benchmark"
+        self.hidden = hiddens.pop()
+        # this step's layer inputs of the new tokens, down-projected into the cache rows by the fused write
+        self.x = torch.randn(self.L, self.B, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
+        self.w_down = [w.kv_latent_proj.to(device) for w in self.weights]
         pos = torch.tensor(seq_lens) - 1
         self.slots = (bt[torch.arange(self.B), pos // page].long() * page + pos % page).to(device)
         self.sched = dec.make_schedule(self.B, device)
@@ -147,7 +150,8 @@ class Workload:
         decode-kernel launch."""
         dec.schedule(self.sched, self.seq_lens)
         for l, lat in enumerate(self.layers):
-            latent_ops.latent_rows_to_cache(self.c[l], self.slots, self.caches[l], lat.u_cat, lat.k_segs_host, lat.eps)
+            latent_ops.project_rows_to_cache(self.x[l], self.w_down[l], self.slots, self.caches[l], lat.u_cat,
+                                             lat.k_segs_host, lat.eps)
             q_bd = lat.block_diag_query(self.q[l])
             part = self.part[:, :, :lat.v_rank + 1]
             if dec_events is not None:
@@ -171,14 +175,15 @@ class Workload:
         return rows + self.B * H * kq * 2
 
     def step_bytes(self) -> int:
-        """Algorithmic bytes of one step (rows, factors, q in, out, new rows), summed over layers."""
+        """Algorithmic bytes of one step, summed over layers: context rows read once, the factors (U_k, U_v and the
+        down-projection W_down), q in and out, the new tokens' inputs and their rows written."""
         tot = 0
         for l, lat in enumerate(self.layers):
             lay = self.weights[l].layout
             rows = sum(self.seq_lens_list) * self.W * 2
-            factors = 2 * (sum(256 * r for r in lay["k_head_ranks"]) + 4 * 256 * lay["v_rank"])
+            factors = 2 * (sum(256 * r for r in lay["k_head_ranks"]) + 4 * 256 * lay["v_rank"] + self.W * self.hidden)
             qo = 2 * self.B * H * D * 2
-            tot += rows + factors + qo + 2 * self.B * self.W
+            tot += rows + factors + qo + 2 * self.B * (self.hidden + self.W)
         return tot
 
 
@@ -347,17 +352,18 @@ def run_reference_arm(args, rank, world):
 
 # ------------------------------------------------------------------------------------------------------------ e2e
 def e2e_rate(wl: Workload, steps: int, warmup: int):
-    """Decode tokens/s through ``LatentAttentionImpl.forward`` with this step's inputs copied from pinned host memory
-    and the outputs copied back inside the timed region."""
+    """Decode tokens/s through the backend's public surface (``latent_attention_step``: the fused down-projection
+    cache write, then ``LatentAttentionImpl.forward``), with this step's inputs (queries, layer inputs of the new
+    tokens, positions) copied from pinned host memory and the attention outputs copied back inside the timed region."""
     from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl,
-                                          LatentAttentionMetadataBuilder, LatentKVSpec)
+                                          LatentAttentionMetadataBuilder, LatentKVSpec, latent_attention_step)
     dev = wl.device
     B, L = wl.B, wl.L
     q_host = wl.q.cpu().pin_memory()
-    c_host = wl.c.cpu().pin_memory()
+    x_host = wl.x.cpu().pin_memory()
     pos_host = (torch.tensor(wl.seq_lens_list) - 1).pin_memory()
     out_host = torch.empty(L, B, H, D, dtype=torch.bfloat16).pin_memory()
-    q_dev, c_dev = torch.empty_like(wl.q), torch.empty_like(wl.c)
+    q_dev, x_dev = torch.empty_like(wl.q), torch.empty_like(wl.x)
     pos_dev = torch.empty(B, dtype=torch.int64, device=dev)
     out_dev = torch.empty(L, B, H, D, dtype=torch.bfloat16, device=dev)
     spec = LatentKVSpec(block_size=wl.page, num_kv_heads=1, head_size=wl.W)
@@ -375,14 +381,14 @@ def e2e_rate(wl: Workload, steps: int, warmup: int):
 
     def one():
         q_dev.copy_(q_host, non_blocking=True)
-        c_dev.copy_(c_host, non_blocking=True)
+        x_dev.copy_(x_host, non_blocking=True)
         pos_dev.copy_(pos_host, non_blocking=True)
         cm = CommonAttentionMetadata(query_start_loc=qsl_dev, query_start_loc_cpu=qsl, seq_lens=wl.seq_lens,
                                      block_table_tensor=wl.block_table, slot_mapping=wl.slots, num_reqs=B,
                                      num_actual_tokens=B, max_query_len=1)
         md = builder.build(0, cm)
         for l in range(L):
-            impl.forward(layer_objs[l], q_dev[l], c_dev[l], pos_dev, kv[:, l], md, out_dev[l])
+            latent_attention_step(impl, layer_objs[l], q_dev[l], x_dev[l], wl.w_down[l], kv[:, l], md, out_dev[l])
         out_host.copy_(out_dev, non_blocking=True)
 
     for _ in range(warmup):
@@ -395,7 +401,7 @@ def e2e_rate(wl: Workload, steps: int, warmup: int):
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
-    h2d = q_host.numel() * 2 + c_host.numel() * 2 + pos_host.numel() * 8
+    h2d = q_host.numel() * 2 + x_host.numel() * 2 + pos_host.numel() * 8
     d2h = out_host.numel() * 2
     return B / (ms / 1000.0), ms, h2d, d2h
 

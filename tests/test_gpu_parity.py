@@ -14,7 +14,7 @@ import oracle
 from belt_b200 import decode as dec
 from belt_b200 import latent_ops, synth
 from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl, LatentAttentionMetadataBuilder,
-                                      LatentKVSpec)
+                                      LatentKVSpec, latent_attention_step)
 from belt_b200.layer import derive_latent_tensors
 
 from conftest import CASES, bf16_ulp_close, golden_case
@@ -379,6 +379,15 @@ def test_backend_forward_decode_step():
     assert bf16_ulp_close(kv_d[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=1)
     assert_close_out(output, exp, "backend forward")
     assert impl.forward(Layer, q.to(DEV), c.to(DEV), pos.to(DEV), kv_d, None, output.clone()).abs().sum() == 0
+
+    # the model-side step with the down-projection fused into the write gives the same rows and output
+    kv_f = kv.to(DEV)
+    out_f = torch.empty_like(output)
+    latent_attention_step(impl, Layer, q.to(DEV), x.to(DEV), w.kv_latent_proj.to(DEV), kv_f, md, out_f)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    assert bf16_ulp_close(kv_f[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=2, atol=PROJ_ATOL)
+    assert_close_out(out_f, exp, "fused step")
 
 
 def test_decode_long_context_properties():
