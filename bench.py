@@ -36,7 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from belt_b200 import decode as dec  # noqa: E402
-from belt_b200 import latent_ops, synth  # noqa: E402
+from belt_b200 import dp, latent_ops, synth  # noqa: E402
 
 METRIC = "decode tokens/s/GPU and % of latent-attn roofline at 1/2/4/8 B200 (DP)"
 H, D = 24, 256
@@ -57,49 +57,22 @@ def parse_args():
     return ap.parse_args()
 
 
-def dist_env():
-    rank = int(os.environ.get("RANK", 0))
-    world = int(os.environ.get("WORLD_SIZE", 1))
-    local = int(os.environ.get("LOCAL_RANK", 0))
-    return rank, world, local
-
-
-def init_dist(world):
-    if world > 1:
-        import torch.distributed as dist
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        from datetime import timedelta
-        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
-        return dist
-    return None
-
-
-def barrier(dist):
-    if dist is not None:
-        dist.barrier()
-
-
-def max_over_ranks(dist, x: float) -> float:
-    if dist is None:
-        return x
-    t = torch.tensor([x], dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
 # ------------------------------------------------------------------------------------------------------------ workload
-def workload_spec(config: int, batch: int | None, rank: int):
-    """(layer specs, seq_lens, page, description) of this rank's share."""
+def workload_spec(config: int, batch: int | None, rank: int, world: int):
+    """(layer specs, this rank's seq_lens, page, description, partition imbalance). The box holds batch x world
+    requests; ranks take LPT shares by context tokens (equal counts), so every rank decodes ~batch requests."""
     if config == 2:
         B = batch or 64
-        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}
+        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}, 1.0
     B = batch or 128
     ranks = synth.learned_ranks(16)
-    lens = synth.log_uniform_lengths(B, 1024, 65536, seed=synth.SEED_LENGTHS + 17 * rank)
+    pool = synth.log_uniform_lengths(B * world, 1024, 65536, seed=synth.SEED_LENGTHS)
+    parts = dp.partition_lpt(pool, world)
+    lens = [pool[i] for i in parts[rank]]
     specs = [synth.spec_from_ranks(rk, rv) for rk, rv in ranks]
     return specs, [L + 1 for L in lens], 16, {
         "workload": "config3: 16 layers, learned ranks (r_k in {384..640}, r_v = 1024 - r_k), batch 128/GPU, "
-                    "context log-uniform [1k, 64k], page 16"}
+                    "context log-uniform [1k, 64k], page 16"}, dp.imbalance(pool, parts)
 
 
 class Workload:
@@ -329,9 +302,11 @@ def _cpu_time(w, lens, page):
 
 
 def run_reference_arm(args, rank, world):
+    """The reference's CPU path on the whole box's requests (every rank's share), rank 0 only."""
     if rank != 0:
         return
-    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, 0)
+    per_gpu = args.batch or (64 if args.config == 2 else 128)
+    specs, seq_lens, page, cfg, _ = workload_spec(args.config, per_gpu * world, 0, 1)
     rates, tsum = [], 0.0
     for i in range(args.warmup + args.steps):
         budget = min(args.cpu_seconds, 240.0 / max(1, args.warmup + args.steps))
@@ -418,16 +393,18 @@ def read_traffic():
 
 def main():
     args = parse_args()
-    rank, world, local = dist_env()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
-    dist = init_dist(world)
+    group = dp.HostGroup()
+    local = group.local_rank
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     from belt_b200 import build as _build
     _build.build()
-    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, rank)
+    specs, seq_lens, page, cfg, imb = workload_spec(args.config, args.batch, rank, world)
     wl = Workload(specs, seq_lens, page, dev, rank)
     torch.cuda.synchronize()
 
@@ -439,10 +416,11 @@ def main():
     dec_events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in range(wl.L)] for _ in range(args.steps)]
     clocks = ClockSampler(dev)
-    barrier(dist)
+    group.barrier()
     clocks.start()
     time.sleep(0.3)
     torch.cuda.synchronize()
+    group.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for k in range(args.steps):
@@ -450,11 +428,12 @@ def main():
     end.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
-    barrier(dist)
+    group.barrier()
     ms_local = start.elapsed_time(end) / args.steps
-    ms = max_over_ranks(dist, ms_local)
+    ms = group.max(ms_local)
     dec.check_device_errors(dev)
-    value = world * wl.B / (ms / 1000.0)
+    total_reqs = group.sum(wl.B)
+    value = total_reqs / (ms / 1000.0)
 
     # the decode kernel's launches, per layer
     peaks = {}
@@ -470,7 +449,7 @@ def main():
     kern_bytes = [wl.decode_kernel_bytes(l) for l in range(wl.L)]
     achieved = sum(kern_bytes) / (sum(kern_ms) / 1000.0) / 1e9
     step_gb = wl.step_bytes() / 1e9
-    step_frac = step_gb / (ms / 1000.0) / peak_gbs
+    step_frac = step_gb / (ms_local / 1000.0) / peak_gbs
     traffic = read_traffic()
     traffic_per_launch = None
     if traffic and traffic.get("bytes_per_context_token"):
@@ -479,8 +458,9 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {**cfg, "global_batch": wl.B * world, "per_gpu_batch": wl.B, "layers": wl.L,
+            "config": {**cfg, "global_batch": int(total_reqs), "per_gpu_batch": wl.B, "layers": wl.L,
                        "context_tokens_per_gpu": sum(wl.seq_lens_list), "parallelism": f"dp{world}",
+                       "partition": "LPT by context tokens, equal request counts", "partition_imbalance": imb,
                        "l2": "inputs larger than L2 (cache %.1f GB per GPU)" % (wl.buf.numel() * 2 / 1e9),
                        "tokens_per_s_per_gpu": value / world,
                        "step_roofline_frac": step_frac, "step_algorithmic_gb": step_gb},
@@ -491,17 +471,16 @@ def main():
             "clocks": clk,
             "gpu_launches": wl.launches_per_step * args.steps}
     if not args.no_e2e:
-        e_rate, e_ms, h2d, d2h = e2e_rate(wl, max(2, args.steps // 2), 2)
-        e_rate = max_over_ranks(dist, e_ms)
-        line["e2e"] = {"value": world * wl.B / (e_rate / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                       "d2h_bytes_per_step": d2h, "ms_per_step": e_rate}
+        _, e_ms_local, h2d, d2h = e2e_rate(wl, max(2, args.steps // 2), 2)
+        e_ms = group.max(e_ms_local)
+        line["e2e"] = {"value": total_reqs / (e_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, desc, t = cpu_reference_rate(specs, seq_lens, page, args.cpu_seconds)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+    group.close()
 
 
 if __name__ == "__main__":
