@@ -47,7 +47,7 @@ constexpr int kKstBytes = 64 * 16 * 2;          // [64 x 16] BF16 = 2 KB
 constexpr int kPBytes = kTile * 32 * 2;         // [128 tokens x 32 heads] BF16 = 8 KB
 constexpr int kThreads = 384;
 constexpr int kRegsWg0 = 80, kRegsWork = 208;   // 80 + 2 * 208 <= 3 * 168 registers per SMSP
-constexpr int kProducerLanes = 4;
+constexpr int kProducerLanes = 16;             // one TMA box per lane and stage (16 boxes of a 128-token stage)
 constexpr int kTmemCols = 512;
 constexpr int kTmemK = 64;
 constexpr int kTmemO = 320;
@@ -67,8 +67,9 @@ constexpr int bPvDone = bPFull + 2;            // [2]
 constexpr int bOFree = bPvDone + 2;
 constexpr int bDrain = bOFree + 1;
 constexpr int bSoft = bDrain + 1;              // softmax group barrier (4 warps)
+constexpr int bImg = bSoft + 1;                // rebuild images written (4 rotation warps)
 constexpr int kNumBars = 32;
-static_assert(bSoft < kNumBars, "barriers");
+static_assert(bImg < kNumBars, "barriers");
 // red_max [2][4][32], red_sum [4][32], flags [2][4], per-head alpha / 1 / sum [32]
 constexpr int kRedFloats = 2 * 4 * 32 + 4 * 32 + 2 * 4 + 32;
 }  // namespace dec
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     mbar_init(&bars[bOFree], 4);
     mbar_init(&bars[bDrain], 1);
     mbar_init(&bars[bSoft], 4);
+    mbar_init(&bars[bImg], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -225,20 +227,6 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     tma_prefetch_desc(&maps.q);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
-  if (warp >= 4 && warp < 8 && has_work) {
-    // rebuild B images: K-step e holds rope_blocks[:, src_e : src_e + 16] as a K-major [64 x 16] no-swizzle operand
-    // (8 x 16-byte core matrices: element (n, k) at (n / 8) * 256 + (k / 8) * 128 + (n % 8) * 16 + (k % 8) * 2)
-    const int t = threadIdx.x - 128;
-    for (int e = 0; e < p.n_kst; ++e) {
-      uint8_t* img = sB + e * kKstBytes;
-      for (int idx = t; idx < 64 * 16; idx += 128) {
-        const int n = idx >> 4, k = idx & 15;
-        const __nv_bfloat16 v = p.rope_blocks[static_cast<long long>(n) * p.rope_ld + p.kst_src[e] + k];
-        *reinterpret_cast<__nv_bfloat16*>(img + (n >> 3) * 256 + (k >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2) = v;
-      }
-    }
-    fence_proxy_async_smem();
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -249,78 +237,88 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
    if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (lanes 0-3)
     if (lane < kProducerLanes && has_work) {
+      constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
       int fills = 0, qsegs = 0;
       bool ok = true;
-      // the boxes of one stage: chunks [chunk0, chunk0 + nch) of the tile's 128 tokens (chunk = 64 columns from
-      // column `col0`); every lane issues every kProducerLanes-th box, lane 0 arms the barrier first
-      auto load_stage = [&](const TileCursor& c, int col0, int chunk0, int nch) -> bool {
+      // Where this lane's box of a tile comes from: chunked layout, tokens [8 lane, 8 lane + 8) of the tile; page
+      // layout, piece lane % n_pieces (of chunk lane / n_pieces). One block-table read per lane and tile; pages past
+      // the request read as block num_blocks, all out of bounds (zeros).
+      struct BoxPos {
+        int blk, row;
+      };
+      auto box_pos = [&](const TileCursor& c) -> BoxPos {
+        const int npages = (__ldg(p.seq_lens + c.si.b) + p.page - 1) / p.page;
+        const int tok0 = c.tile * kTile + (kChunked ? 8 * lane : (lane % p.n_pieces) * p.box_rows);
+        const int pg = tok0 / p.page;
+        BoxPos bp{p.num_blocks, tok0 - pg * p.page};
+        if (pg < npages) bp.blk = __ldg(p.block_table + static_cast<long long>(c.si.b) * p.bt_stride + pg);
+        return bp;
+      };
+      // one stage: chunks [chunk0, chunk0 + nch) (column col0 on), lane 0 waits for the slot and arms its barrier,
+      // then every lane issues its box in the same instruction
+      auto load_stage = [&](const BoxPos& bp, int col0, int chunk0, int nch) -> bool {
         const int st = fills % S;
         const int rnd = fills / S;
-        const bool got =
-            rnd == 0 || mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
-        if (!__all_sync(0xFu, got)) return false;
+        bool got = true;
+        if (lane == 0 && rnd > 0)
+          got = mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
+        if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) return false;
         if (lane == 0) mbar_arrive_expect_tx(&bars[bFull + st], nch * kTile * 128);
-        __syncwarp(0xFu);
+        __syncwarp(kLanes);
         uint8_t* dst = ring + st * p.stage_bytes;
-        const int seq = __ldg(p.seq_lens + c.si.b);
-        const int npages = (seq + p.page - 1) / p.page;
-        const int32_t* bt = p.block_table + static_cast<long long>(c.si.b) * p.bt_stride;
         if constexpr (kChunked) {
-          for (int b = lane; b < kTile / 8; b += kProducerLanes) {   // 8 tokens per box
-            const int tok0 = c.tile * kTile + 8 * b;
-            const int pg = tok0 / p.page;
-            const int blk = pg < npages ? __ldg(bt + pg) : p.num_blocks;   // past the request: all-OOB (zeros)
-            tma_load_4d(dst + b * p.atom_stride, &maps.cache[nch - 1], &bars[bFull + st], 0, tok0 - pg * p.page,
-                        chunk0, blk);
-          }
-        } else {
-          for (int i = lane; i < nch * p.n_pieces; i += kProducerLanes) {
-            const int h = i / p.n_pieces, pc = i - h * p.n_pieces;
-            const int tok0 = c.tile * kTile + pc * p.box_rows;
-            const int pg = tok0 / p.page;
-            const int blk = pg < npages ? __ldg(bt + pg) : p.num_blocks;
-            tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st],
-                        col0 + 64 * h, tok0 - pg * p.page, blk);
-          }
+          tma_load_4d(dst + lane * p.atom_stride, &maps.cache[nch - 1], &bars[bFull + st], 0, bp.row, chunk0, bp.blk);
+        } else if (lane < nch * p.n_pieces) {
+          const int h = lane / p.n_pieces, pc = lane - h * p.n_pieces;
+          tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st],
+                      col0 + 64 * h, bp.row, bp.blk);
         }
         ++fills;
         return true;
       };
-      auto load_K = [&](const TileCursor& c) -> bool {
-        if (c.first()) {
-          const bool got = qsegs == 0 ||
-                           mbar_wait(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
-          if (!__all_sync(0xFu, got)) return false;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
-            for (int ch = 0; ch < p.n_k + kG; ++ch)
-              tma_load_2d(sQ + ch * kQChunkBytes, &maps.q, &bars[bQFull], ch * 64, c.si.b * kH);
-          }
-          ++qsegs;
-        }
-        for (int k = 0; k < p.n_ks; ++k)
-          if (!load_stage(c, 64 * p.cps * k, p.cps * k, min(p.cps, p.n_k - p.cps * k))) return false;
-        return true;
-      };
-      auto load_V = [&](const TileCursor& c) -> bool {
-        for (int k = 0; k < p.n_vs; ++k)
-          if (!load_stage(c, p.v_offset + 64 * p.cps * k, p.v_chunk0 + p.cps * k, min(p.cps, p.n_vc - p.cps * k)))
-            return false;
+      // the segment's query chunks, one per lane
+      auto load_q = [&](const TileCursor& c) -> bool {
+        bool got = true;
+        if (lane == 0 && qsegs > 0)
+          got = mbar_wait(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
+        if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) return false;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
+        __syncwarp(kLanes);
+        if (lane < p.n_k + kG) tma_load_2d(sQ + lane * kQChunkBytes, &maps.q, &bars[bQFull], lane * 64, c.si.b * kH);
+        ++qsegs;
         return true;
       };
       TileCursor kc, vc;
       kc.begin(p, seg_begin, seg_end);
       vc.begin(p, seg_begin, seg_end);
+      BoxPos pos_k{}, pos_v{};
+      auto load_K = [&]() -> bool {
+        if (kc.first() && !load_q(kc)) return false;
+        pos_k = box_pos(kc);
+        for (int k = 0; k < p.n_ks; ++k)
+          if (!load_stage(pos_k, 64 * p.cps * k, p.cps * k, min(p.cps, p.n_k - p.cps * k))) return false;
+        return true;
+      };
+      auto load_V = [&](const BoxPos& bp) -> bool {
+        for (int k = 0; k < p.n_vs; ++k)
+          if (!load_stage(bp, p.v_offset + 64 * p.cps * k, p.v_chunk0 + p.cps * k, min(p.cps, p.n_vc - p.cps * k)))
+            return false;
+        return true;
+      };
+      // stage order K(0), K(1), V(0), K(2), V(1), ...: V(i) reuses the box positions computed for K(i)
       if (kc.valid) {
-        ok = load_K(kc);
+        ok = load_K();
+        pos_v = pos_k;
         kc.next(p);
       }
       while (ok && vc.valid) {
+        const BoxPos cur_v = pos_v;
         if (kc.valid) {
-          if (!(ok = load_K(kc))) break;
+          if (!(ok = load_K())) break;
+          pos_v = pos_k;
           kc.next(p);
         }
-        if (!(ok = load_V(vc))) break;
+        if (!(ok = load_V(cur_v))) break;
         vc.next(p);
       }
       if (lane == 0 && *abort_flag) {
@@ -444,7 +442,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       TileCursor kc, vc;
       kc.begin(p, seg_begin, seg_end);
       vc.begin(p, seg_begin, seg_end);
-      if (kc.valid) {
+      ok = wait(bImg, 0);   // the rotation warps' rebuild images
+      if (ok && kc.valid) {
         ok = mma_K(kc, 0) && mma_rope(kc, 0);
         kc.next(p);
       }
@@ -470,6 +469,30 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     // ------------------------------------------------------------------ rotation warps: RoPE keys
     warpgroup_reg_alloc<kRegsWork>();
     if (has_work) {
+      {
+        // rebuild B images: K-step e holds rope_blocks[:, src_e : src_e + 16] as a K-major [64 x 16] no-swizzle
+        // operand (8 x 16-byte core matrices: element (n, k) at (n / 8) * 256 + (k / 8) * 128 + (n % 8) * 16 +
+        // (k % 8) * 2). 16-byte pieces (K-step, row, 8-column half), all loads issued before the stores; built while
+        // the first stages stream in, the MMA issuer waits for bImg before its first rebuild.
+        const int t = threadIdx.x - 128;
+        uint4 v[kDecodeMaxKsteps];
+#pragma unroll
+        for (int e = 0; e < kDecodeMaxKsteps; ++e)
+          if (e < p.n_kst) {
+            const int n = t >> 1, h = t & 1;
+            v[e] = __ldg(reinterpret_cast<const uint4*>(p.rope_blocks + static_cast<long long>(n) * p.rope_ld +
+                                                         p.kst_src[e] + 8 * h));
+          }
+#pragma unroll
+        for (int e = 0; e < kDecodeMaxKsteps; ++e)
+          if (e < p.n_kst) {
+            const int n = t >> 1, h = t & 1;
+            *reinterpret_cast<uint4*>(sB + e * kKstBytes + (n >> 3) * 256 + h * 128 + (n & 7) * 16) = v[e];
+          }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[bImg]);
+      }
       const int quad = warp & 3;
       const int row = quad * 32 + lane;
       const uint32_t tK = tmem + (static_cast<uint32_t>(quad * 32) << 16) + kTmemK;
