@@ -424,6 +424,7 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   p.stage_bytes = p.cps * 128 * 128;
   p.n_ks = (n_k + p.cps - 1) / p.cps;
   p.n_vs = (p.n_vc + p.cps - 1) / p.cps;
+  // rows per TMA box: a whole page up to 128 rows (chunked boxes stack 8-row groups, page boxes are plain rows)
   p.box_rows = page < 128 ? page : 128;
   p.n_pieces = 128 / p.box_rows;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
@@ -498,13 +499,16 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
 
   DecodeMaps maps;
   if (use_chunked) {
-    // {64 columns, page rows, 64-column chunks, blocks}; box {64, 8, n, 1} for n = 1..4 chunks
-    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(page), static_cast<cuuint64_t>(row_chunks),
+    // {64 columns, 8 rows, 64-column chunks, 8-row groups of a page, blocks}; box {64, 8, n, box_rows / 8, 1} for
+    // n = 1..4 chunks: the chunk index sits between the rows of a group and the groups, so each 8-row group of the box
+    // lands as one n-chunk atom in shared memory
+    cuuint64_t dims[5] = {64, 8, static_cast<cuuint64_t>(row_chunks), static_cast<cuuint64_t>(page / 8),
                           static_cast<cuuint64_t>(num_blocks)};
-    cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride_tok) * 2, 128, static_cast<cuuint64_t>(stride_block) * 2};
+    cuuint64_t strides[4] = {static_cast<cuuint64_t>(stride_tok) * 2, 128, static_cast<cuuint64_t>(stride_tok) * 16,
+                             static_cast<cuuint64_t>(stride_block) * 2};
     for (int n = 1; n <= 4; ++n) {
-      cuuint32_t box[4] = {64, 8, static_cast<cuuint32_t>(n), 1};
-      int r = encode_bf16(&maps.cache[n - 1], cache, 4, dims, strides, box, "cache");
+      cuuint32_t box[5] = {64, 8, static_cast<cuuint32_t>(n), static_cast<cuuint32_t>(p.box_rows / 8), 1};
+      int r = encode_bf16(&maps.cache[n - 1], cache, 5, dims, strides, box, "cache");
       if (r != BELT_OK) return r;
     }
   } else {

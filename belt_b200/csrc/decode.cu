@@ -155,6 +155,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, "
+      "%7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
 // Element i (BF16) of 8 x 16 bytes held in registers, as fp32 (i is a compile-time constant after unrolling).
 __device__ __forceinline__ float bf16_lane(const uint4 (&v)[8], int i) {
   const uint4 q = v[i >> 3];
@@ -240,15 +249,15 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
       int fills = 0, qsegs = 0;
       bool ok = true;
-      // Where this lane's box of a tile comes from: chunked layout, tokens [8 lane, 8 lane + 8) of the tile; page
-      // layout, piece lane % n_pieces (of chunk lane / n_pieces). One block-table read per lane and tile; pages past
-      // the request read as block num_blocks, all out of bounds (zeros).
+      // Where this lane's box of a tile comes from: chunked layout, tokens [box_rows lane, box_rows (lane + 1)) of the
+      // tile (lanes < n_pieces); page layout, piece lane % n_pieces (of chunk lane / n_pieces). One block-table read
+      // per lane and tile; pages past the request read as block num_blocks, all out of bounds (zeros).
       struct BoxPos {
         int blk, row;
       };
       auto box_pos = [&](const TileCursor& c) -> BoxPos {
         const int npages = (__ldg(p.seq_lens + c.si.b) + p.page - 1) / p.page;
-        const int tok0 = c.tile * kTile + (kChunked ? 8 * lane : (lane % p.n_pieces) * p.box_rows);
+        const int tok0 = c.tile * kTile + (kChunked ? lane : lane % p.n_pieces) * p.box_rows;
         const int pg = tok0 / p.page;
         BoxPos bp{p.num_blocks, tok0 - pg * p.page};
         if (pg < npages) bp.blk = __ldg(p.block_table + static_cast<long long>(c.si.b) * p.bt_stride + pg);
@@ -267,7 +276,11 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         __syncwarp(kLanes);
         uint8_t* dst = ring + st * p.stage_bytes;
         if constexpr (kChunked) {
-          tma_load_4d(dst + lane * p.atom_stride, &maps.cache[nch - 1], &bars[bFull + st], 0, bp.row, chunk0, bp.blk);
+          // 5-D box {64 columns, 8 rows, nch chunks, box_rows / 8 row groups, 1 block}: every 8-row group lands one atom
+          // (nch chunks of 1 KB) after the previous one, so a stage's atoms are nch KB apart
+          if (lane < p.n_pieces)
+            tma_load_5d(dst + lane * (p.box_rows / 8) * nch * p.chunk_stride, &maps.cache[nch - 1], &bars[bFull + st], 0,
+                        0, chunk0, bp.row / 8, bp.blk);
         } else if (lane < nch * p.n_pieces) {
           const int h = lane / p.n_pieces, pc = lane - h * p.n_pieces;
           tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st],
@@ -347,7 +360,6 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         return true;
       };
       // Descriptors (16-byte units): every operand's high word is fixed, a K step only moves the low word.
-      const uint32_t hiSw = desc_hi(p.atom_stride, kSwizzle128);     // cache chunks: SBO = 8-token atom stride
       constexpr uint32_t hiQ = desc_hi(1024, kSwizzle128);          // query chunks: 8 rows = 1 KB
       constexpr uint32_t hiImg = desc_hi(256, kSwizzleNone);        // rebuild images: 8 rows = 256 B
       constexpr uint32_t hiP = desc_hi(128, kSwizzleNone);          // P: 8 heads = 128 B
@@ -356,7 +368,10 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       const uint32_t loQ = desc_lo(q_a, 16);                        // + chunk * 192, + step * 2
       const uint32_t loImg = desc_lo(b_a, 128);                     // + e * 128
       const uint32_t loP = desc_lo(p_a, 512);                       // + buffer * 512, + step * 64
-      const uint32_t stage16 = p.stage_bytes >> 4, chunk16 = p.chunk_stride >> 4, pv_step16 = (2 * p.atom_stride) >> 4;
+      const uint32_t stage16 = p.stage_bytes >> 4, chunk16 = p.chunk_stride >> 4;
+      // chunked layout: a stage of nch chunks holds 8-token atoms of nch KB (the producer's boxes stack them densely);
+      // page layout: chunks of 128 rows, atoms of 1 KB whatever the stage holds
+      auto atom_of = [&](int nch) -> int { return kChunked ? nch * p.chunk_stride : p.atom_stride; };
       // key part of tile i: scores into S[i & 1] and the rebuilt RoPE keys
       auto mma_K = [&](const TileCursor& c, int i) -> bool {
         if (c.first()) {
@@ -374,6 +389,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
           if (!full(st)) return false;
           const uint32_t a0 = loRing + st * stage16;
           const int c0 = p.cps * k, c1 = min(p.n_k, c0 + p.cps);
+          const uint32_t hiSw = desc_hi(atom_of(c1 - c0), kSwizzle128);
           for (int cc = c0; cc < c1; ++cc) {
             const uint32_t ac = a0 + (cc - c0) * chunk16;
             const uint32_t bq = loQ + cc * (kQChunkBytes >> 4);
@@ -423,6 +439,9 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
           int st;
           if (!full(st)) return false;
           const uint32_t a0 = loRingV + st * stage16;
+          const int nchv = min(p.cps, p.n_vc - p.cps * k);
+          const uint32_t hiSw = desc_hi(atom_of(nchv), kSwizzle128);
+          const uint32_t pv_step16 = (2 * atom_of(nchv)) >> 4;
           const int j0 = (p.cps * k) >> 1, j1 = min(p.n_vp, (p.cps * (k + 1)) >> 1);
           for (int j = j0; j < j1; ++j) {
             const uint32_t aj = a0 + (2 * j - p.cps * k) * chunk16;

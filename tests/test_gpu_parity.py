@@ -314,6 +314,22 @@ def test_decode_page_sizes_and_strided_views(page):
     assert not out[6].float().abs().any()                     # a padded request (length 0) gives zeros
 
 
+@pytest.mark.parametrize("r_k", [384, 448, 512, 576, 640])
+@pytest.mark.parametrize("page", [16, 64])
+def test_decode_learned_ranks(r_k, page):
+    """Every per-layer rank split of the 16-layer config (r_v = 1024 - r_k): key and value parts whose chunk counts
+    leave partial stages (n_k = 6, 7, 9, 10; 6..10 value chunks), against the fp32 oracle."""
+    spec = synth.spec_from_ranks(r_k, 1024 - r_k)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=3000)
+    seqs = [2049, 1, 700, 129, 1500]
+    batch = synth.make_batch(w.layout, seqs, page=page, seed=21)
+    q = synth.make_queries(len(seqs), seed=22)
+    out, *_ = run_decode(lat, q.to(DEV), batch.cache.to(DEV), batch.block_table.to(DEV), batch.seq_lens.to(DEV))
+    exp = oracle.decode_fp32(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+    assert_close_out(out, exp, f"r_k {r_k}, page {page}")
+
+
 def test_decode_invariances():
     """Bit-identical under a permutation of physical blocks; within tolerance across different CTA counts."""
     spec = synth.spec_from_ranks(448, 576)
