@@ -453,6 +453,19 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
       ks_list[j] = ks_list[j - 1];
       ks_list[j - 1] = t;
     }
+  for (int g = 0; g < kG; ++g) {
+    const int off = rope_groups[2 * g], rr = rope_groups[2 * g + 1];
+    p.rope_ks0[g] = off / 16;
+    p.rope_ks1[g] = (off + rr - 1) / 16;
+    p.rope_e0[g] = -1;
+    for (int e = 0; e < nk; ++e)
+      if (ks_list[e].group == g && ks_list[e].col == 16 * p.rope_ks0[g]) p.rope_e0[g] = e;
+    for (int j = 0; j <= p.rope_ks1[g] - p.rope_ks0[g]; ++j) {
+      const int e = p.rope_e0[g] + j;
+      if (p.rope_e0[g] < 0 || e >= nk || ks_list[e].group != g || ks_list[e].col != 16 * (p.rope_ks0[g] + j))
+        return fail(BELT_ERR_INVALID, "latent_decode: RoPE coordinates of group %d interleave with another group's", g);
+    }
+  }
   for (int e = 0; e < nk; ++e) {
     p.kst_col[e] = ks_list[e].col;
     p.kst_src[e] = ks_list[e].src;

@@ -89,7 +89,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 100000)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
     if (clock64() - t0 > kWaitCycles) {
       if (err) atomicCAS(err, 0, code);
@@ -162,24 +162,25 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] x B[smem desc]
+// D[tmem] (+)= A[smem desc] x B[smem desc]. No memory clobber: the operands are ordered by the mbarrier waits and
+// fences before the issue and the tcgen05.commit after it (volatile asm keeps that order), and a clobber would make
+// the compiler reload every memory-resident value (kernel parameters included) between two MMA issues, which costs
+// more than the tensor core's ~45 cycles per small MMA.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
-// D[tmem] (+)= A[tmem] x B[smem desc]
+// D[tmem] (+)= A[tmem] x B[smem desc] (no memory clobber, as mma_ss)
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                        uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 // Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.

@@ -397,11 +397,21 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             for (int s16 = 0; s16 < 4; ++s16)
               mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
           }
-          for (int e = p.ks_kst_begin[k]; e < p.ks_kst_end[k]; ++e) {
-            const int col = p.kst_col[e];
-            const uint32_t ac = a0 + ((col >> 6) - c0) * chunk16 + ((col & 63) >> 3);
-            mma_ss(tmem + kTmemK + 64 * p.kst_group[e], desc_of(ac, hiSw), desc_of(loImg + e * (kKstBytes >> 4), hiImg),
-                   idK, p.kst_first[e] ? 0u : 1u);
+          // RoPE-key rebuild: every group's 16-column steps that fall in this stage's chunks (constant parameter offsets
+          // only, so nothing but arithmetic sits between two MMA issues)
+#pragma unroll
+          for (int g = 0; g < kG; ++g) {
+            const int ks0 = p.rope_ks0[g];
+            const int lo = max(ks0, 4 * c0), hi = min(p.rope_ks1[g], 4 * c1 - 1);
+            const uint32_t dK = tmem + kTmemK + 64 * g;
+            uint64_t da = desc_of(a0 + (lo / 4 - c0) * chunk16 + (lo % 4) * 2, hiSw);
+            uint64_t db = desc_of(loImg + (p.rope_e0[g] + lo - ks0) * (kKstBytes >> 4), hiImg);
+            for (int ks = lo; ks <= hi; ++ks) {
+              mma_ss(dK, da, db, idK, ks != ks0 ? 1u : 0u);
+              // next 16 columns: +32 bytes along the swizzled row, or the start of the next chunk
+              da += (ks % 4 == 3) ? chunk16 - 6 : 2;
+              db += kKstBytes >> 4;
+            }
           }
           mma_commit(&bars[bEmpty + st]);
           ++fills;

@@ -40,6 +40,9 @@ struct DecodeParams {
   int kst_group[kDecodeMaxKsteps];
   int kst_first[kDecodeMaxKsteps];
   int ks_kst_begin[8], ks_kst_end[8];  // rebuild K-steps (sorted by column) inside each key stage
+  // per group: first and last 16-column step holding its RoPE coordinates, and the image of the first step (the
+  // steps of a group are consecutive images)
+  int rope_ks0[4], rope_ks1[4], rope_e0[4];
   float scale_log2;
   // shared-memory layout (byte offsets from the 1024-aligned base), set by the host launcher
   int stages;
