@@ -544,6 +544,12 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
 }
 
+int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream) {
+  if (!err || !status) return fail(BELT_ERR_INVALID, "selftest_bounded_wait: null buffer");
+  cudaError_t e = belt::launch_selftest_wait(err, status, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "selftest_bounded_wait launch");
+}
+
 int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
                         int32_t num_reqs, int32_t nh, int32_t lv, void* out, int64_t out_sb, int64_t out_sh,
                         float* lse, int64_t lse_sb, void* stream) {

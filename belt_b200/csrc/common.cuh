@@ -26,6 +26,7 @@ enum DeviceError : int {
   kErrTimeoutMma = 0x102,
   kErrTimeoutEpilogue = 0x103,
   kErrBadSegment = 0x110,
+  kErrTimeoutSelftest = 0x1F0,
 };
 
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 2 GHz: far above any legitimate wait

@@ -161,6 +161,9 @@ struct ProjWriteParams {
 };
 cudaError_t launch_proj_write(const ProjWriteMaps& maps, const ProjWriteParams& p, cudaStream_t stream);
 
+// Bounded-wait self-test (selftest.cu).
+cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);
+
 // Sets the text belt_last_error() returns on the calling thread.
 void set_last_error(const char* msg);
 

@@ -151,6 +151,14 @@ int belt_latent_decode_noalloc(const void* q_bd, int32_t num_reqs, int32_t kq, c
                                const void* cos_sin, int32_t max_pos, void* out, int64_t out_sb, int64_t out_sh,
                                float* lse, int64_t lse_sb, int32_t* err, void* stream);
 
+/*
+ * Self-test of the kernels' bounded waits (no counterpart in the reference): launches one thread that waits on a
+ * barrier nothing completes. The wait gives up after the same limit the decode kernel uses (~2 s), writes 0x1F0 into
+ * the device word `err` (if still 0), and the kernel ends normally; status (device int32[2]) receives {2, 1} (wait gave
+ * up, abort flag raised). For tests of failure detection: the CUDA context stays usable afterwards.
+ */
+int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream);
+
 /* Number of SMs of `device` (the decode grid: one CTA per SM). */
 int belt_num_sms(int32_t device);
 
