@@ -100,6 +100,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait for a thread that has nothing else to do meanwhile and is not on the critical path: it sleeps `ns`
+// nanoseconds between polls, so a long wait does not take issue slots from the warps that share its scheduler.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code,
+                                               uint32_t ns) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      if (err) atomicCAS(err, 0, code);
+      *abort = 1;
+      return false;
+    }
+    __nanosleep(ns);
+  }
+  return true;
+}
+
 // Bounded wait that no abort flag cuts short (for waits that must see in-flight work finish, e.g. before freeing
 // TMEM). Records `code` in *err (if given) and returns false after `limit` cycles.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code,

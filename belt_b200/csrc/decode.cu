@@ -5,14 +5,14 @@
 // semantics, 128-token tiles). Twelve warps in three warpgroups; warpgroup 0 gives registers to the other two
 // (setmaxnreg: 80 / 208 / 208 per thread, within the 3 x 168 the launch provides):
 //
-// * warp 0, TMA producer (lanes 0-3 share the boxes of a stage): streams the cache through a ring of stages, each
-//   `cps` 64-column chunks of 128 tokens, all SWIZZLE_128B. Two layouts:
-//     - chunked (64-column-aligned row parts): 4-D boxes of 8 rows x n chunks (one box per 8 tokens, 4 KB for 4
-//       chunks, 512 contiguous bytes per row); a chunk's 8-token atoms sit 4 KB apart. Four lanes issuing 4 KB boxes
-//       keep the HBM near its copy bandwidth, where one lane issuing 2 KB boxes tops out near a third of it;
+// * warp 0, TMA producer (lanes 0-15, one box per lane and stage, issued in one instruction): streams the cache
+//   through a ring of stages, each `cps` 64-column chunks of 128 tokens, all SWIZZLE_128B. Two layouts:
+//     - chunked (64-column-aligned row parts): one 5-D box {64 columns, 8 rows, n chunks, 8-row groups, 1 block} per
+//       page (16 rows x 4 chunks = 8 KB at page 16), the 8-row groups landing as consecutive atoms of n KB;
 //     - page (any 8-aligned layout): 3-D boxes of `page` rows x 64 columns, 2 chunks per stage.
-//   Pages past the request are all-OOB boxes (zeros). Stage order is software-pipelined across tiles: K(0), K(1), V(0),
-//   K(2), V(1), ... so that tile i's softmax runs while tile i+1's key stages are scored and tile i's values stream in.
+//   Each lane reads its box's block id once per tile. Pages past the request are all-OOB boxes (zeros). Stage order is
+//   software-pipelined across tiles: K(0), K(1), V(0), K(2), V(1), ... so that tile i's softmax runs while tile i+1's
+//   key stages are scored and tile i's values stream in.
 // * warp 1, tcgen05 issuer (one thread; descriptors advance only their low words), M = 128 tokens:
 //     - scores S[tok, head] (N = 32: 24 heads; the last 8 columns are ignored) over the K part against the
 //       block-diagonal query;
@@ -20,7 +20,8 @@
 //       resident [64 x 16] images of the rope blocks (N = 64), into TMEM;
 //     - after the rotation warps wrote the rotated BF16 keys back into TMEM, the RoPE score with A read from TMEM;
 //     - O^T[latent, head] += V^T P per 128-latent block (A = the cache stage read MN-major, B = P from shared memory).
-// * warps 2-3: idle.
+// * warp 2, query loader (lanes 0-15): a segment's block-diagonal query chunks, once the previous segment released them.
+// * warp 3: idle.
 // * warps 4-7, rotation: BF16(gain * B_g c~) -> NeoX rotation at each token's position in fp32 -> BF16 operand
 //   (cute_decode.py:473-484), one TMEM lane (token) per thread.
 // * warps 8-11, softmax: masked online softmax in the exp2 domain; the running max of a head is raised only when a
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     // ------------------------------------------------------------------ TMA producer (lanes 0-3)
     if (lane < kProducerLanes && has_work) {
       constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
-      int fills = 0, qsegs = 0;
+      int fills = 0;
       bool ok = true;
       // Where this lane's box of a tile comes from: chunked layout, tokens [box_rows lane, box_rows (lane + 1)) of the
       // tile (lanes < n_pieces); page layout, piece lane % n_pieces (of chunk lane / n_pieces). One block-table read
@@ -289,24 +290,11 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         ++fills;
         return true;
       };
-      // the segment's query chunks, one per lane
-      auto load_q = [&](const TileCursor& c) -> bool {
-        bool got = true;
-        if (lane == 0 && qsegs > 0)
-          got = mbar_wait(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
-        if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) return false;
-        if (lane == 0) mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
-        __syncwarp(kLanes);
-        if (lane < p.n_k + kG) tma_load_2d(sQ + lane * kQChunkBytes, &maps.q, &bars[bQFull], lane * 64, c.si.b * kH);
-        ++qsegs;
-        return true;
-      };
       TileCursor kc, vc;
       kc.begin(p, seg_begin, seg_end);
       vc.begin(p, seg_begin, seg_end);
       BoxPos pos_k{}, pos_v{};
       auto load_K = [&]() -> bool {
-        if (kc.first() && !load_q(kc)) return false;
         pos_k = box_pos(kc);
         for (int k = 0; k < p.n_ks; ++k)
           if (!load_stage(pos_k, 64 * p.cps * k, p.cps * k, min(p.cps, p.n_k - p.cps * k))) return false;
@@ -318,7 +306,9 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             return false;
         return true;
       };
-      // stage order K(0), K(1), V(0), K(2), V(1), ...: V(i) reuses the box positions computed for K(i)
+      // stage order K(0), K(1), V(0), K(2), V(1), ...: V(i) reuses the box positions computed for K(i). (Taking V(i)
+      // before K(i + 1) where tile i + 1 opens a segment was measured 4 % slower: the MMA issuer then idles while the
+      // softmax finishes tile i, with the ring full of value stages.)
       if (kc.valid) {
         ok = load_K();
         pos_v = pos_k;
@@ -337,7 +327,6 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       if (lane == 0 && *abort_flag) {
         // let every copy issued land before the CTA's shared memory goes away
         for (int k = max(0, fills - S); k < fills; ++k) mbar_wait_drain(&bars[bFull + k % S], (k / S) & 1);
-        if (qsegs > 0) mbar_wait_drain(&bars[bQFull], (qsegs - 1) & 1);
       }
     }
     __syncwarp();
@@ -492,8 +481,30 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       }
     }
     __syncwarp();
+   } else if (warp == 2) {
+    // ------------------------------------------------------------------ query loader (lanes 0-15): the segment's
+    // block-diagonal query chunks, one per lane, as soon as the previous segment's last RoPE score released them
+    if (lane < kProducerLanes && has_work) {
+      constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
+      int qsegs = 0;
+      TileCursor c;
+      c.begin(p, seg_begin, seg_end);
+      for (; c.valid; c.next(p)) {
+        if (!c.first()) continue;
+        bool got = true;
+        if (lane == 0 && qsegs > 0)   // waits a whole segment: sleep between polls
+          got = mbar_wait_idle(&bars[bQEmpty], (qsegs - 1) & 1, abort_flag, p.err, kErrTimeoutProducer, 256);
+        if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) break;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[bQFull], (p.n_k + kG) * kQChunkBytes);
+        __syncwarp(kLanes);
+        if (lane < p.n_k + kG) tma_load_2d(sQ + lane * kQChunkBytes, &maps.q, &bars[bQFull], lane * 64, c.si.b * kH);
+        ++qsegs;
+      }
+      if (lane == 0 && *abort_flag && qsegs > 0) mbar_wait_drain(&bars[bQFull], (qsegs - 1) & 1);
+    }
+    __syncwarp();
    }
-   // warps 2-3: no role
+   // warp 3: no role
   } else if (warp < 8) {
     // ------------------------------------------------------------------ rotation warps: RoPE keys
     warpgroup_reg_alloc<kRegsWork>();
