@@ -108,7 +108,9 @@ int run_group_product(const belt::GroupGemmParams& gp, const char* what, cudaStr
         hp.run_hi[g][i] = gp.run_hi[g][i];
       }
     }
-    hp.nb = 2;
+    // column tile: 128 columns for the wide absorbed query (most tiles are outside the runs and only write zeros),
+    // 64 for the 256-column U_v projection (more CTAs for its deeper K loop)
+    hp.nb = gp.N <= 256 ? 1 : 2;
     hp.vec_out = aligned16(gp.Out) && gp.sot % 8 == 0 && gp.soh % 8 == 0;
     hp.err = nullptr;
     e = belt::launch_head_gemm(maps, hp, stream);
@@ -319,10 +321,12 @@ int belt_latent_proj_rows_to_cache(const void* x, int64_t num_tokens, int64_t x_
     }
     p.item_nch[items++] = n;
   }
-  for (int c = lk >> 6; c < (row_width + 63) >> 6; c += 4) {
+  // V part in windows of two 64-column chunks: more CTAs, each streaming a smaller share of W_down
+  constexpr int kVChunks = 2;
+  for (int c = lk >> 6; c < (row_width + 63) >> 6; c += kVChunks) {
     if (items == belt::kPwMaxItems)
       return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: V part too wide (%d columns)", row_width - lk);
-    const int n = ((row_width + 63) >> 6) - c < 4 ? ((row_width + 63) >> 6) - c : 4;
+    const int n = ((row_width + 63) >> 6) - c < kVChunks ? ((row_width + 63) >> 6) - c : kVChunks;
     for (int i = 0; i < n; ++i) p.item_chunk[items][i] = c + i;
     p.item_nch[items++] = n;
   }

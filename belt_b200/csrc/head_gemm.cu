@@ -49,8 +49,15 @@ __global__ void __launch_bounds__(kHgThreads, 1)
   bool any = false;
   for (int i = 0; i < p.nruns[g]; ++i) any |= p.run_lo[g][i] < n0 + BN && p.run_hi[g][i] > n0;
   if (!any) {   // no live column: zeros (uniform over the CTA, decided before any barrier or TMEM use)
-    if (row < p.T)
-      for (int c = 0; c < BN && n0 + c < p.N; ++c) out_row[n0 + c] = __float2bfloat16_rn(0.f);
+    if (row < p.T) {
+      if (p.vec_out && n0 + BN <= p.N) {
+        uint4* dst = reinterpret_cast<uint4*>(out_row + n0);
+#pragma unroll
+        for (int q = 0; q < BN / 8; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        for (int c = 0; c < BN && n0 + c < p.N; ++c) out_row[n0 + c] = __float2bfloat16_rn(0.f);
+      }
+    }
     return;
   }
 

@@ -138,7 +138,7 @@ cudaError_t launch_cache_write(const CacheWriteParams& p, cudaStream_t stream);
 // Work items: KV groups 0..G-1, then chunks of the V part [lk, W); item i covers the 64-column chunks
 // item_chunk[i][0 .. item_nch[i]) of the row (ascending).
 constexpr int kPwMaxChunks = 5;
-constexpr int kPwMaxItems = 12;
+constexpr int kPwMaxItems = 16;
 struct ProjWriteMaps {
   CUtensorMap x;
   CUtensorMap w;
