@@ -427,3 +427,31 @@ def test_decode_long_context_properties():
     alone, *_ = run_decode(lat, q[37:38], cache, bt[37:38].to(DEV), sl[37:38])
     err = (alone.float() - out[37:38].float()).abs()
     assert float(err.max()) < MAX_ABS
+
+
+@pytest.mark.parametrize("spec_name", ["c50", "c25"])
+def test_decode_config4_long_context(spec_name):
+    """Config 4 shapes at full size (32 requests x 65,537 tokens, page 16; c50 rows of 1,024 columns and the c25
+    variant of 512): 512 tiles per request spread over every CTA. Finite, two requests against the fp32 oracle,
+    the same outputs from a 7-CTA split (other segments, other merges), and a request decoded alone."""
+    spec = getattr(synth, spec_name)()
+    w = synth.make_layer(spec)
+    L = 65537
+    lat, ref = layer_pair(w, max_pos=L)
+    seqs = [L] * 32
+    bt, nb, _ = synth.block_tables(seqs, 16)
+    cache = torch.empty(nb, 16, w.layout["row_width"], dtype=torch.bfloat16, device=DEV)
+    synth.fill_cache(cache, w.layout, bt.to(DEV), seqs, seed=41, poison=False)
+    q = synth.make_queries(32, seed=42).to(DEV)
+    sl = torch.tensor(seqs, dtype=torch.int32, device=DEV)
+    out, *_ = run_decode(lat, q, cache, bt.to(DEV), sl)
+    assert torch.isfinite(out.float()).all()
+    sample = [3, 30]
+    cpu_cache = cache.cpu()
+    exp = oracle.decode_fp32(q[sample].cpu(), cpu_cache, bt[sample], torch.tensor([L] * 2), ref, SCALE)
+    assert_close_out(out[sample], exp, f"{spec_name} long-context sample")
+    out7, *_ = run_decode(lat, q, cache, bt.to(DEV), sl, num_ctas=7)
+    err = (out7.float() - out.float()).abs()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS
+    alone, *_ = run_decode(lat, q[30:31], cache, bt[30:31].to(DEV), sl[30:31])
+    assert float((alone.float() - out[30:31].float()).abs().max()) < MAX_ABS
