@@ -128,6 +128,20 @@ def _side_stream(device: torch.device) -> torch.cuda.Stream:
     return stream
 
 
+def _write_rows(m: LatentAttentionMetadata, device, write):
+    """Run ``write`` (this step's cache rows): on the side stream when the step has ``SIDE_STREAM_MIN_DECODES`` decodes
+    or more (it then overlaps the absorbed query; the caller joins the returned stream before reading the cache), else
+    on the current stream (returns None)."""
+    if m.num_decodes >= SIDE_STREAM_MIN_DECODES:
+        main, side = torch.cuda.current_stream(device), _side_stream(device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            write()
+        return side
+    write()
+    return None
+
+
 class LatentAttentionMetadataBuilder:
     """Per-step metadata; fills the step's decode schedule once (latent_backend.py:148-225)."""
 
@@ -206,24 +220,26 @@ class LatentAttentionImpl:
         if attn_metadata is None:                 # profiling run
             return output.fill_(0)
         m = attn_metadata
-        lat: LatentLayer = layer.latent
-        cache = kv_cache[:, 0]                    # [blocks, block_size, row_width], strided per block
-        nd = m.num_decode_tokens
         slots = m.slot_mapping
         side = None
         if slots is not None and key is not None:
-            if m.num_decodes >= SIDE_STREAM_MIN_DECODES:
-                main, side = torch.cuda.current_stream(query.device), _side_stream(query.device)
-                side.wait_stream(main)
-                with torch.cuda.stream(side):
-                    self.do_kv_cache_update(layer, key, value, kv_cache, slots)
-            else:
-                self.do_kv_cache_update(layer, key, value, kv_cache, slots)
+            side = _write_rows(m, query.device, lambda: self.do_kv_cache_update(layer, key, value, kv_cache, slots))
+        return self._attend(layer, query, kv_cache, m, output, side)
+
+    def _attend(self, layer, query: torch.Tensor, kv_cache: torch.Tensor, m: LatentAttentionMetadata,
+                output: torch.Tensor, side) -> torch.Tensor:
+        """Decode and prefill attention of the step; ``side`` is the stream still writing this step's rows (or None):
+        the decode waits for it after the absorbed query, which does not read the cache."""
+        lat: LatentLayer = layer.latent
+        cache = kv_cache[:, 0]                    # [blocks, block_size, row_width], strided per block
+        nd = m.num_decode_tokens
+        main = torch.cuda.current_stream(query.device)
         if m.num_decodes:
             dev = query.device
             q_bd = lat.block_diag_query(query[:nd])
             if side is not None:
                 main.wait_stream(side)            # the step's own rows are part of the context
+                side = None
             part = torch.empty(nd + m.sched.num_ctas, self.num_heads, lat.v_rank + 1, dtype=torch.float32,
                                device=dev)
             a = torch.empty(nd, self.num_heads, lat.v_rank, dtype=query.dtype, device=dev)
@@ -232,6 +248,8 @@ class LatentAttentionImpl:
                               lat.v_offset, lat.v_rank, rope=lat.rope)
             dec.merge_segments(part, m.sched, a, lse)
             lat.up_project(a, output[:nd])
+        if side is not None:
+            main.wait_stream(side)
         if m.num_prefills:
             self._prefill(lat, query, output, cache, m)
         return output
@@ -278,14 +296,17 @@ def latent_attention_step(impl: "LatentAttentionImpl", layer, query: torch.Tenso
     ``key = kv_latent_proj(hidden)``, then the backend's cache write and attention), with the down-projection fused
     into the cache write: the rows of every scheduled token (``attn_metadata.slot_mapping``) are computed from
     ``hidden`` [T, hidden_size] and ``w_down`` (``kv_latent_proj.weight`` [>= row_width, hidden_size]) and written in
-    one kernel, then ``impl.forward`` attends with ``key=None`` (nothing left to write)."""
+    one kernel (on the side stream at ``SIDE_STREAM_MIN_DECODES`` decodes, overlapping the absorbed query, as
+    ``LatentAttentionImpl.forward`` does with its cache write), then attends as ``impl.forward``."""
     if attn_metadata is None:
         return output.fill_(0)
     lat: LatentLayer = layer.latent
-    if attn_metadata.slot_mapping is not None:
-        latent_ops.project_rows_to_cache(hidden, w_down, attn_metadata.slot_mapping, kv_cache[:, 0], lat.u_cat,
-                                         lat.k_segs_host, lat.eps)
-    return impl.forward(layer, query, None, None, kv_cache, attn_metadata, output)
+    m = attn_metadata
+    side = None
+    if m.slot_mapping is not None:
+        side = _write_rows(m, query.device, lambda: latent_ops.project_rows_to_cache(
+            hidden, w_down, m.slot_mapping, kv_cache[:, 0], lat.u_cat, lat.k_segs_host, lat.eps))
+    return impl._attend(layer, query, kv_cache, m, output, side)
 
 
 class LatentAttentionBackend:

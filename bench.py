@@ -112,6 +112,7 @@ class Workload:
         pos = torch.tensor(seq_lens) - 1
         self.slots = (bt[torch.arange(self.B), pos // page].long() * page + pos % page).to(device)
         self.sched = dec.make_schedule(self.B, device)
+        self.side = torch.cuda.Stream(device)
         self.part = torch.empty(self.B + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
         self.a = torch.empty(self.B, H, 640, dtype=torch.bfloat16, device=device)
         self.lse = torch.empty(self.B, H, dtype=torch.float32, device=device)
@@ -122,10 +123,15 @@ class Workload:
         """One decode step over all layers through the operator API; ``dec_events`` [(start, end)] brackets every
         decode-kernel launch."""
         dec.schedule(self.sched, self.seq_lens)
+        main = torch.cuda.current_stream(self.device)
         for l, lat in enumerate(self.layers):
-            latent_ops.project_rows_to_cache(self.x[l], self.w_down[l], self.slots, self.caches[l], lat.u_cat,
-                                             lat.k_segs_host, lat.eps)
+            # the new rows on the side stream, overlapping the absorbed query (the backend's side-stream write)
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                latent_ops.project_rows_to_cache(self.x[l], self.w_down[l], self.slots, self.caches[l], lat.u_cat,
+                                                 lat.k_segs_host, lat.eps)
             q_bd = lat.block_diag_query(self.q[l])
+            main.wait_stream(self.side)
             part = self.part[:, :, :lat.v_rank + 1]
             if dec_events is not None:
                 dec_events[l][0].record()
