@@ -369,8 +369,9 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         }
         const int sb = i & 1;
         if (i >= 2 && !wait(bSFree + sb, ((i >> 1) - 1) & 1)) return false;
-        // the previous tile's RoPE-score MMAs read the rotated keys from the TMEM columns the rebuild overwrites
-        if (i >= 1 && !wait(bSFull + ((i - 1) & 1), ((i - 1) >> 1) & 1)) return false;
+        // The previous tile's RoPE-score MMAs read the rotated keys from the TMEM columns this tile's rebuild
+        // overwrites: they were issued before, and tcgen05.mma operations of one thread execute in issue order, so
+        // no wait (a wait here would drain the tensor pipe once per tile).
         tc_fence_after();
         const uint32_t dS = tmem + 32 * sb;
         for (int k = 0; k < p.n_ks; ++k) {
