@@ -17,6 +17,7 @@ c_i32p = ctypes.POINTER(ctypes.c_int32)
 # name -> argument types (all return int status)
 SIGNATURES = {
     "belt_decode_schedule": [c_vp, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
+    "belt_decode_schedule_weighted": [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
     "belt_block_diag_query": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32p, c_vp, c_vp],
     "belt_up_project": [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp],
     "belt_latent_rows_to_cache": [c_vp, c_i64, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp,

@@ -150,8 +150,24 @@ int belt_decode_schedule(const int32_t* seq_lens, int32_t num_reqs, int32_t num_
   if (work_capacity < static_cast<int64_t>(num_reqs) + num_ctas)
     return fail(BELT_ERR_INVALID, "schedule: work capacity %lld < num_reqs + num_ctas = %lld",
                 (long long)work_capacity, (long long)num_reqs + num_ctas);
-  belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, work, work_capacity, cta_seg,
-                         seg_base, err};
+  belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, 1, 0, work, work_capacity,
+                         cta_seg, seg_base, err};
+  cudaError_t e = belt::launch_schedule(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "schedule launch");
+}
+
+int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                                  int32_t start_cost, int32_t* work, int64_t work_capacity, int32_t* cta_seg,
+                                  int32_t* seg_base, int32_t* err, void* stream) {
+  if (num_reqs < 0 || num_ctas < 1) return fail(BELT_ERR_INVALID, "schedule: num_reqs %d, num_ctas %d", num_reqs, num_ctas);
+  if (start_cost < 0 || start_cost > 1024) return fail(BELT_ERR_INVALID, "schedule: start_cost %d outside [0, 1024]", start_cost);
+  if ((num_reqs > 0 && !seq_lens) || !work || !cta_seg || !seg_base)
+    return fail(BELT_ERR_INVALID, "schedule: null buffer");
+  if (work_capacity < static_cast<int64_t>(num_reqs) + num_ctas)
+    return fail(BELT_ERR_INVALID, "schedule: work capacity %lld < num_reqs + num_ctas = %lld",
+                (long long)work_capacity, (long long)num_reqs + num_ctas);
+  belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, 8, start_cost, work,
+                         work_capacity, cta_seg, seg_base, err};
   cudaError_t e = belt::launch_schedule(p, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "schedule launch");
 }

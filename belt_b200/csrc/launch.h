@@ -97,6 +97,7 @@ cudaError_t launch_head_gemm(const HeadGemmMaps& maps, HeadGemmParams p, cudaStr
 struct ScheduleParams {
   const int32_t* seq_lens;
   int num_reqs, num_ctas, min_tiles, tile;
+  int unit, start_cost;   // cost of a tile and extra cost of a request's first tile (1, 0: the reference's split)
   int32_t* work;
   long long work_capacity;
   int32_t* cta_seg;

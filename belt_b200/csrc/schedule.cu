@@ -1,9 +1,11 @@
 // Split-KV work schedule of one decode step, computed on the device (graph-safe: fixed grid, persistent buffers).
 //
-// Same split as the reference's ``_schedule`` (plugins/vllm_lrkv/vllm_lrkv/cute_decode.py:571-607): every request's
-// context is cut into `tile`-token tiles, the tiles of the whole batch (request order) are dealt out in equal runs of
-// per = max(ceil(total / num_ctas), min_tiles, 1) tiles to the CTAs, and a run that crosses request boundaries
-// becomes several segments:
+// With unit 1 and start cost 0 this is the reference's ``_schedule`` split (plugins/vllm_lrkv/vllm_lrkv/
+// cute_decode.py:571-607): every request's context is cut into `tile`-token tiles, the tiles of the whole batch
+// (request order) are dealt out in equal runs of per = max(ceil(total / num_ctas), min_tiles, 1) tiles to the CTAs,
+// and a run that crosses request boundaries becomes several segments. The weighted split (unit 8, start cost s) deals
+// out cost instead: a tile costs 8 units and every request's first tile s more, so that a CTA which switches between
+// requests (a query reload and a partial-output epilogue per switch) gets fewer tiles. In both:
 //   work[k]     = (request, first tile, end tile, 0), segments in request order;
 //   seg_base[b] = first segment of request b, seg_base[B] = number of segments;
 //   cta_seg[c]  = first segment of CTA c, cta_seg[num_ctas] = number of segments.
@@ -49,57 +51,70 @@ __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleP
   __shared__ long long total_s;
   const int B = p.num_reqs;
   const int tile = p.tile;
-  // pass 1: first global tile of every request (kept in seg_base until pass 2 overwrites it)
+  const long long u = p.unit, s0 = p.start_cost;
+  // pass 1: cost offset of every request (kept in seg_base until pass 2 overwrites it) and the total cost
   long long carry = 0;
   for (int b0 = 0; b0 < B; b0 += kSchedThreads) {
     const int b = b0 + threadIdx.x;
     const long long tiles = b < B ? (static_cast<long long>(p.seq_lens[b]) + tile - 1) / tile : 0;
-    const long long ex = block_exclusive_scan(tiles, warp_sums, &total_s);
+    const long long cost = tiles > 0 ? s0 + u * tiles : 0;
+    const long long ex = block_exclusive_scan(cost, warp_sums, &total_s);
     if (b < B) p.seg_base[b] = static_cast<int32_t>(carry + ex);
     carry += total_s;
     __syncthreads();
   }
-  const long long total_tiles = carry;
-  long long per = (total_tiles + p.num_ctas - 1) / p.num_ctas;
-  per = per > p.min_tiles ? per : p.min_tiles;
-  per = per > 1 ? per : 1;
-  // pass 2: segments
+  const long long total_cost = carry;
+  long long per = (total_cost + p.num_ctas - 1) / p.num_ctas;
+  per = per > u * p.min_tiles ? per : u * p.min_tiles;
+  per = per > u ? per : u;
+  auto cdiv = [](long long a, long long b) { return a >= 0 ? (a + b - 1) / b : -((-a) / b); };
+  // pass 2: segments. Tile k of request b starts at cost x_b + s0 + u k (x_b: the request's cost offset) and belongs
+  // to CTA floor(cost / per); consecutive tiles of one request on one CTA form a segment.
   long long seg_carry = 0;
   for (int b0 = 0; b0 < B; b0 += kSchedThreads) {
     const int b = b0 + threadIdx.x;
-    long long tiles = 0, first = 0, nseg = 0;
+    long long tiles = 0, x = 0, nseg = 0, c0 = 0;
     if (b < B) {
       tiles = (static_cast<long long>(p.seq_lens[b]) + tile - 1) / tile;
-      first = p.seg_base[b];
-      nseg = tiles > 0 ? (first + tiles - 1) / per - first / per + 1 : 0;
+      x = p.seg_base[b];
+      if (tiles > 0) {
+        c0 = (x + s0) / per;
+        nseg = (x + s0 + u * (tiles - 1)) / per - c0 + 1;
+      }
     }
     const long long base = seg_carry + block_exclusive_scan(nseg, warp_sums, &total_s);
     if (b < B) {
       p.seg_base[b] = static_cast<int32_t>(base);
-      const long long cta0 = first / per;
+      if (nseg > 0) {
+        // CTAs after the previous request's last tile up to this one's first start at this request's first segment
+        const long long prev = x > 0 ? (x - u) / per : -1;
+        for (long long c = prev + 1; c <= c0 && c <= p.num_ctas; ++c) p.cta_seg[c] = static_cast<int32_t>(base);
+      }
       for (long long j = 0; j < nseg; ++j) {
-        const long long cta = cta0 + j;
-        const long long g0 = first > cta * per ? first : cta * per;
-        const long long e = first + tiles;
-        const long long g1 = e < (cta + 1) * per ? e : (cta + 1) * per;
+        const long long cta = c0 + j;
+        long long k0 = cdiv(cta * per - x - s0, u), k1 = cdiv((cta + 1) * per - x - s0, u);
+        k0 = k0 > 0 ? k0 : 0;
+        k1 = k1 < tiles ? k1 : tiles;
         const long long k = base + j;
         if (k < p.work_capacity) {
           p.work[4 * k + 0] = b;
-          p.work[4 * k + 1] = static_cast<int32_t>(g0 - first);
-          p.work[4 * k + 2] = static_cast<int32_t>(g1 - first);
+          p.work[4 * k + 1] = static_cast<int32_t>(k0);
+          p.work[4 * k + 2] = static_cast<int32_t>(k1);
           p.work[4 * k + 3] = 0;
         } else if (p.err) {
           atomicCAS(p.err, 0, kErrBadSegment);
         }
-        if (g0 == cta * per && cta <= p.num_ctas) p.cta_seg[cta] = static_cast<int32_t>(k);
+        if (j > 0 && cta <= p.num_ctas) p.cta_seg[cta] = static_cast<int32_t>(k);
       }
     }
     seg_carry += total_s;
     __syncthreads();
   }
   if (threadIdx.x == 0) p.seg_base[B] = static_cast<int32_t>(seg_carry);
-  for (int c = threadIdx.x; c <= p.num_ctas; c += kSchedThreads)
-    if (static_cast<long long>(c) * per >= total_tiles) p.cta_seg[c] = static_cast<int32_t>(seg_carry);
+  // CTAs after the last tile (and every CTA when there are no tiles) start at the end
+  const long long last = total_cost > 0 ? (total_cost - u) / per : -1;
+  for (long long c = last + 1 + threadIdx.x; c <= p.num_ctas; c += kSchedThreads)
+    p.cta_seg[c] = static_cast<int32_t>(seg_carry);
 }
 
 cudaError_t launch_schedule(const ScheduleParams& p, cudaStream_t stream) {

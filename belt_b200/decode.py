@@ -64,35 +64,50 @@ class DecodeSchedule:
     work: torch.Tensor
     cta_seg: torch.Tensor           # [num_ctas + 1] int32
     seg_base: torch.Tensor          # [max_reqs + 1] int32
+    # 0: the reference's split (equal runs of tiles); > 0: equal runs of cost, a tile costing 8 and a request's first
+    # tile this much more (belt_decode_schedule_weighted)
+    start_cost: int = 0
 
     @property
     def capacity(self) -> int:
         return self.work.shape[0]
 
 
-def make_schedule(max_reqs: int, device, num_ctas: int | None = None) -> DecodeSchedule:
-    """Buffers for up to ``max_reqs`` decode requests; one CTA per SM by default (cute_decode.py:562-568)."""
+# Extra cost of a request's first tile in the weighted split, in eighths of a tile: a segment switch costs the decode
+# kernel a query reload and a partial-output epilogue, measured at about one tile's time.
+SCHEDULE_START_COST = 10
+
+
+def make_schedule(max_reqs: int, device, num_ctas: int | None = None,
+                  start_cost: int = SCHEDULE_START_COST) -> DecodeSchedule:
+    """Buffers for up to ``max_reqs`` decode requests; one CTA per SM by default (cute_decode.py:562-568).
+    ``start_cost`` 0 keeps the reference's split; the default weights request starts (``DecodeSchedule``)."""
     device = torch.device(device)
     if num_ctas is None:
         num_ctas = torch.cuda.get_device_properties(device).multi_processor_count
     i32 = dict(device=device, dtype=torch.int32)
     return DecodeSchedule(num_ctas, torch.zeros(max_reqs + num_ctas, 4, **i32), torch.zeros(num_ctas + 1, **i32),
-                          torch.zeros(max_reqs + 1, **i32))
+                          torch.zeros(max_reqs + 1, **i32), int(start_cost))
 
 
 def schedule(sched: DecodeSchedule, seq_lens: torch.Tensor, min_tiles: int = 1) -> None:
     """Fill ``sched`` for the decode requests ``seq_lens`` [B] (int32, on the device): runs of
-    max(ceil(tiles / num_ctas), ``min_tiles``) tiles per CTA; a request of length 0 gets no segment
-    (cute_decode.py:601-607)."""
+    max(ceil(tiles / num_ctas), ``min_tiles``) tiles per CTA (cute_decode.py:601-607), or with
+    ``sched.start_cost`` > 0 runs of equal cost; a request of length 0 gets no segment."""
     B = seq_lens.shape[0]
     if B + 1 > sched.seg_base.shape[0]:
         raise ValueError(f"schedule: {B} requests exceed the schedule's capacity {sched.seg_base.shape[0] - 1}")
     if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
         raise ValueError("schedule: seq_lens must be contiguous int32")
     dev = seq_lens.device
-    _lib.call("belt_decode_schedule", seq_lens.data_ptr(), B, sched.num_ctas, min_tiles, sched.work.data_ptr(),
-              sched.work.shape[0], sched.cta_seg.data_ptr(), sched.seg_base.data_ptr(), error_word(dev).data_ptr(),
-              _stream_ptr(dev))
+    if sched.start_cost > 0:
+        _lib.call("belt_decode_schedule_weighted", seq_lens.data_ptr(), B, sched.num_ctas, min_tiles,
+                  sched.start_cost, sched.work.data_ptr(), sched.work.shape[0], sched.cta_seg.data_ptr(),
+                  sched.seg_base.data_ptr(), error_word(dev).data_ptr(), _stream_ptr(dev))
+    else:
+        _lib.call("belt_decode_schedule", seq_lens.data_ptr(), B, sched.num_ctas, min_tiles, sched.work.data_ptr(),
+                  sched.work.shape[0], sched.cta_seg.data_ptr(), sched.seg_base.data_ptr(),
+                  error_word(dev).data_ptr(), _stream_ptr(dev))
 
 
 def block_diag_query(q_lat: torch.Tensor, q_rot: torch.Tensor, k_off: list, k_ranks: list, lk_pad: int,

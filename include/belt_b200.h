@@ -45,6 +45,17 @@ int belt_decode_schedule(const int32_t* seq_lens, int32_t num_reqs, int32_t num_
                          void* stream);
 
 /*
+ * The cost-weighted variant of belt_decode_schedule (no reference counterpart; same outputs and capacities): a tile
+ * costs 8 units and every request's first tile start_cost (0..1024) more, and the CTAs get equal runs of cost
+ * (max(ceil(total / num_ctas), 8 * min_tiles, 8) units) instead of equal runs of tiles. A CTA that switches between
+ * requests pays a query reload and a partial-output epilogue per switch in the decode kernel; charging start_cost
+ * (about one tile, 8) per request start gives such CTAs fewer tiles, so that the CTAs finish together.
+ */
+int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                                  int32_t start_cost, int32_t* work, int64_t work_capacity, int32_t* cta_seg,
+                                  int32_t* seg_base, int32_t* err, void* stream);
+
+/*
  * Absorbed block-diagonal decode query: replaces latent_ops.py:67-73 (`block_diag_query`, the grouped GEMM of
  * :23-44). q [T, 24, 256] BF16 (element strides q_st, q_sh; last dim contiguous) x qmap [4, 256, kq] BF16
  * (contiguous) -> q_bd [T, 24, kq] BF16 (contiguous). Only the columns listed in col_runs are computed for each

@@ -30,7 +30,7 @@ __all__ = [
     "H", "G", "D", "ROT", "CHUNK", "HPG", "ALIGN", "align", "k_segments", "row_layout", "rope_basis",
     "build_latent_layer", "rope_cos_sin", "derive", "rope_blocks", "latent_rows", "project_rows", "block_diag_query",
     "block_diag_query_construct", "up_project", "decompress", "attend", "gather_rows", "decode_reference",
-    "decode_fp32", "schedule", "decode_partials", "merge_segments", "decode_kernel_path",
+    "decode_fp32", "schedule", "schedule_weighted", "decode_partials", "merge_segments", "decode_kernel_path",
 ]
 
 
@@ -345,6 +345,45 @@ def schedule(seq_lens, num_ctas, tile, min_tiles=1, capacity=None):
     for c in range(num_ctas + 1):
         if c * per >= total_tiles:
             cta_seg[c] = total
+    return work, cta_seg, seg_base
+
+
+def schedule_weighted(seq_lens, num_ctas, tile, start_cost, min_tiles=1, capacity=None):
+    """The cost-weighted split of the decode kernel's schedule (this package's own refinement of
+    ``cute_decode.py:571-607``): tiles in request order cost 8 units each and every request's first tile
+    ``start_cost`` more; CTA c takes the tiles whose cost starts in [c * per, (c + 1) * per), per = max(ceil(total
+    cost / num_ctas), 8 * min_tiles, 8); a CTA's tiles of one request form one segment. Same outputs as ``schedule``
+    (which this equals for start_cost 0 only up to the unit: use ``schedule`` for the reference's split). Written
+    tile by tile, independently of the kernel's closed forms."""
+    seq = np.asarray(seq_lens, dtype=np.int64).reshape(-1)
+    B = seq.shape[0]
+    capacity = capacity or (B + num_ctas)
+    tiles = (seq + tile - 1) // tile
+    total_cost = int(sum(start_cost + 8 * t for t in tiles if t > 0))
+    per = max(-(-total_cost // num_ctas), 8 * min_tiles, 8)
+    segs = []                                   # (request, cta, first tile, end tile)
+    cost = 0
+    for b in range(B):
+        t = int(tiles[b])
+        if t == 0:
+            continue
+        cost += start_cost
+        for k in range(t):
+            cta = cost // per
+            if segs and segs[-1][0] == b and segs[-1][1] == cta:
+                segs[-1][3] = k + 1
+            else:
+                segs.append([b, cta, k, k + 1])
+            cost += 8
+    work = np.zeros((capacity, 4), dtype=np.int32)
+    cta_seg = np.zeros(num_ctas + 1, dtype=np.int32)
+    seg_base = np.zeros(B + 1, dtype=np.int32)
+    for k, (b, cta, k0, k1) in enumerate(segs):
+        work[k] = (b, k0, k1, 0)
+    for b in range(B + 1):
+        seg_base[b] = sum(1 for sg in segs if sg[0] < b)
+    for c in range(num_ctas + 1):
+        cta_seg[c] = sum(1 for sg in segs if sg[1] < c)
     return work, cta_seg, seg_base
 
 

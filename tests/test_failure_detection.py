@@ -29,7 +29,7 @@ def test_bounded_wait_runs_out_and_context_survives():
     assert int(err.item()) == 0x1F0           # the code reached the host through the error word
     # the context is still usable: a regular kernel of the library runs and gives the right answer
     seqs = [300, 0, 129]
-    sched = dec.make_schedule(len(seqs), dev, num_ctas=4)
+    sched = dec.make_schedule(len(seqs), dev, num_ctas=4, start_cost=0)
     dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=dev))
     torch.cuda.synchronize(dev)
     _, cta_seg, seg_base = oracle.schedule(seqs, 4, dec.TILE_T)

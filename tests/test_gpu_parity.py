@@ -63,11 +63,32 @@ def assert_close_out(out, ref, what=""):
     (list(range(0, 3000, 7)), 148),
 ])
 def test_schedule_bit_exact(seqs, nct):
+    """The reference's split (start_cost 0)."""
     B = len(seqs)
-    sched = dec.make_schedule(B, DEV, num_ctas=nct)
+    sched = dec.make_schedule(B, DEV, num_ctas=nct, start_cost=0)
     sched.work.fill_(-7)
     dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
     work, cta_seg, seg_base = oracle.schedule(seqs, nct, dec.TILE_T)
+    total = int(seg_base[-1])
+    torch.cuda.synchronize()
+    assert torch.equal(sched.seg_base.cpu(), torch.from_numpy(seg_base))
+    assert torch.equal(sched.cta_seg.cpu(), torch.from_numpy(cta_seg))
+    assert torch.equal(sched.work[:total].cpu(), torch.from_numpy(work[:total]))
+
+
+@pytest.mark.parametrize("start_cost", [1, dec.SCHEDULE_START_COST, 16, 1024])
+@pytest.mark.parametrize("seqs,nct", [
+    ([129, 513, 1025, 2001], 148), ([1, 17, 129, 300], 8), ([0, 64, 0, 65, 4096, 1], 16), ([8192] * 64, 148),
+    ([5], 148), ([0, 0], 4), ([3000, 1, 1, 1, 7000, 64, 63, 65], 148), ([200] * 300, 148), ([128, 256, 127], 1),
+    (list(range(0, 3000, 7)), 148),
+])
+def test_schedule_weighted_bit_exact(seqs, nct, start_cost):
+    """The cost-weighted split against the oracle's tile-by-tile restatement."""
+    B = len(seqs)
+    sched = dec.make_schedule(B, DEV, num_ctas=nct, start_cost=start_cost)
+    sched.work.fill_(-7)
+    dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
+    work, cta_seg, seg_base = oracle.schedule_weighted(seqs, nct, dec.TILE_T, start_cost)
     total = int(seg_base[-1])
     torch.cuda.synchronize()
     assert torch.equal(sched.seg_base.cpu(), torch.from_numpy(seg_base))

@@ -190,3 +190,34 @@ def test_schedule_invariants():
                 assert segs[0][1] == 0 and segs[-1][2] == tiles and (segs[:, 0] == b).all()
                 assert (segs[1:, 1] == segs[:-1, 2]).all()
             assert cta_seg[0] == 0 and cta_seg[nct] == total and (cta_seg[1:] >= cta_seg[:-1]).all()
+
+
+def test_schedule_weighted_invariants():
+    """The cost-weighted split: every tile covered once and in order, contiguous CTA runs, at most B + num_ctas
+    segments, start cost 0 splitting like the reference split of 8-unit tiles, and a CTA holding request starts never
+    getting more tiles than the cost bound allows."""
+    g = torch.Generator().manual_seed(5)
+    for trial in range(20):
+        B = int(torch.randint(1, 200, (1,), generator=g))
+        seqs = torch.randint(0, 5000, (B,), generator=g).tolist()
+        nct = int(torch.randint(1, 160, (1,), generator=g))
+        for start_cost in (0, 3, 10, 40):
+            work, cta_seg, seg_base = oracle.schedule_weighted(seqs, nct, 128, start_cost)
+            total = int(seg_base[B])
+            assert total <= B + nct
+            for b in range(B):
+                segs = work[seg_base[b]:seg_base[b + 1]]
+                tiles = math.ceil(seqs[b] / 128)
+                if tiles == 0:
+                    assert len(segs) == 0
+                    continue
+                assert segs[0][1] == 0 and segs[-1][2] == tiles and (segs[:, 0] == b).all()
+                assert (segs[1:, 1] == segs[:-1, 2]).all() and (segs[:, 2] > segs[:, 1]).all()
+            assert cta_seg[0] == 0 and cta_seg[nct] == total and (cta_seg[1:] >= cta_seg[:-1]).all()
+            # cost per CTA (8 per tile + start_cost per request start it holds) stays within per + one tile
+            cost_total = sum(start_cost + 8 * math.ceil(L / 128) for L in seqs if L > 0)
+            per = max(-(-cost_total // nct), 8)
+            for c in range(nct):
+                segs = work[cta_seg[c]:cta_seg[c + 1]]
+                cost = sum(8 * int(s[2] - s[1]) + (start_cost if s[1] == 0 else 0) for s in segs)
+                assert cost <= per + 8 + start_cost, (c, cost, per)

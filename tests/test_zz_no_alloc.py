@@ -100,7 +100,7 @@ def _case(r_k, r_v, seqs, seed):
 def _regular(lat, q_bd, cache, bt, seq_lens, num_ctas):
     """The same step through the entry points that take their scratch from the caller."""
     B = q_bd.shape[0]
-    sched = dec.make_schedule(B, q_bd.device, num_ctas=num_ctas)
+    sched = dec.make_schedule(B, q_bd.device, num_ctas=num_ctas, start_cost=0)   # the no-alloc entry's split
     dec.schedule(sched, seq_lens)
     part = torch.full((B + num_ctas, 24, lat.v_rank + 1), float("nan"), device=q_bd.device)
     dec.latent_decode(q_bd, cache, bt, seq_lens, sched, part, SCALE, lat.v_offset, lat.v_rank, rope=lat.rope)
