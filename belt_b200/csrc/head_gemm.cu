@@ -22,12 +22,28 @@ constexpr int kHgABytes = 128 * 128;   // 128 tokens x 64 k x 2 B
 constexpr int kHgBBlock = 64 * 128;    // 64 k x 64 columns x 2 B
 constexpr int kHgMaxStages = 4;
 
-__device__ __forceinline__ bool col_live(const HeadGemmParams& p, int g, int n) {
-  bool live = false;
+// The column runs of one group in registers (empty runs as [0, 0)): the epilogue tests columns against them often,
+// and the parameter arrays are indexed by the group, which is not a compile-time constant.
+struct Runs {
+  int lo[3], hi[3];
+  __device__ Runs(const HeadGemmParams& p, int g) {
 #pragma unroll
-  for (int i = 0; i < 3; ++i) live |= i < p.nruns[g] && n >= p.run_lo[g][i] && n < p.run_hi[g][i];
-  return live;
-}
+    for (int i = 0; i < 3; ++i) {
+      const bool v = i < p.nruns[g];
+      lo[i] = v ? p.run_lo[g][i] : 0;
+      hi[i] = v ? p.run_hi[g][i] : 0;
+    }
+  }
+  __device__ bool live(int n) const {
+    return (n >= lo[0] && n < hi[0]) || (n >= lo[1] && n < hi[1]) || (n >= lo[2] && n < hi[2]);
+  }
+  __device__ bool all_live(int n0, int n1) const {   // [n0, n1) inside one run
+    return (lo[0] <= n0 && n1 <= hi[0]) || (lo[1] <= n0 && n1 <= hi[1]) || (lo[2] <= n0 && n1 <= hi[2]);
+  }
+  __device__ bool all_dead(int n0, int n1) const {   // [n0, n1) meets no run
+    return (hi[0] <= n0 || lo[0] >= n1) && (hi[1] <= n0 || lo[1] >= n1) && (hi[2] <= n0 || lo[2] >= n1);
+  }
+};
 }  // namespace
 
 template <int NB>
@@ -46,9 +62,8 @@ __global__ void __launch_bounds__(kHgThreads, 1)
   const int row = t0 + threadIdx.x;   // this thread's token in the epilogue
   __nv_bfloat16* out_row = p.Out + static_cast<long long>(row) * p.sot + static_cast<long long>(h) * p.soh;
 
-  bool any = false;
-  for (int i = 0; i < p.nruns[g]; ++i) any |= p.run_lo[g][i] < n0 + BN && p.run_hi[g][i] > n0;
-  if (!any) {   // no live column: zeros (uniform over the CTA, decided before any barrier or TMEM use)
+  const Runs runs(p, g);
+  if (runs.all_dead(n0, n0 + BN)) {   // no live column: zeros (uniform over the CTA, before any barrier or TMEM use)
     if (row < p.T) {
       if (p.vec_out && n0 + BN <= p.N) {
         uint4* dst = reinterpret_cast<uint4*>(out_row + n0);
@@ -142,26 +157,26 @@ __global__ void __launch_bounds__(kHgThreads, 1)
       tmem_ld_wait();
       if (row >= p.T) continue;
       const int nb = n0 + c0;
-      // vector stores when the 32 columns lie inside one run (then all are live) and inside the row
-      bool inside = false;
+      // per 8 columns: one 16-byte store when they are all live (values) or all dead (zeros) and inside the row
 #pragma unroll
-      for (int i = 0; i < 3; ++i) inside |= i < p.nruns[g] && p.run_lo[g][i] <= nb && nb + 32 <= p.run_hi[g][i];
-      if (inside && nb + 32 <= p.N && p.vec_out) {
-        uint4* dst = reinterpret_cast<uint4*>(out_row + nb);
+      for (int q = 0; q < 4; ++q) {
+        const int n8 = nb + 8 * q;
+        const bool live8 = runs.all_live(n8, n8 + 8), dead8 = runs.all_dead(n8, n8 + 8);
+        if ((live8 || dead8) && n8 + 8 <= p.N && p.vec_out) {
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (live8) {
+            v.x = pack_bf16(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+            v.y = pack_bf16(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+            v.z = pack_bf16(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+            v.w = pack_bf16(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+          }
+          *reinterpret_cast<uint4*>(out_row + n8) = v;
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 v;
-          v.x = pack_bf16(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-          v.y = pack_bf16(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-          v.z = pack_bf16(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-          v.w = pack_bf16(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-          dst[q] = v;
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int n = nb + i;
-          if (n < p.N) out_row[n] = __float2bfloat16_rn(col_live(p, g, n) ? __uint_as_float(r[i]) : 0.f);
+          for (int i = 0; i < 8; ++i) {
+            const int n = n8 + i;
+            if (n < p.N) out_row[n] = __float2bfloat16_rn(runs.live(n) ? __uint_as_float(r[8 * q + i]) : 0.f);
+          }
         }
       }
     }

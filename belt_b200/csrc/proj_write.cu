@@ -41,9 +41,7 @@ __device__ __forceinline__ long long pw_slot(const ProjWriteParams& p, int t) {
   return (s >= 0 && s < p.num_slots) ? s : -1;
 }
 
-__device__ __forceinline__ bool in_runs(const ProjWriteParams& p, int g, int col) {
-  return (col >= p.a_lo[g] && col < p.a_lo[g] + p.a_n[g]) || (col >= p.b_lo[g] && col < p.b_lo[g] + p.b_n[g]);
-}
+
 
 // Offset of 16-byte unit `u` (8 columns) of token row `r` in a K-major 128-byte-swizzled tile.
 __device__ __forceinline__ int sw128(int r, int u) { return r * 128 + ((u ^ (r & 7)) << 4); }
@@ -61,7 +59,13 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   const int t0 = blockIdx.x * 128, item = blockIdx.y;
   const bool group = item < p.G;
   const int g = item;
+  // the group's two runs in registers (the epilogues test many columns; the arrays are indexed by the item)
+  const int a_lo = group ? p.a_lo[g] : 0, a_hi = group ? a_lo + p.a_n[g] : 0;
+  const int b_lo = group ? p.b_lo[g] : 0, b_hi = group ? b_lo + p.b_n[g] : 0;
+  auto in_runs = [&](int col) { return (col >= a_lo && col < a_hi) || (col >= b_lo && col < b_hi); };
   const int nch = p.item_nch[item];
+  const int win_lo = p.item_chunk[item][0];
+  const bool win_contig = p.item_chunk[item][nch - 1] - win_lo == nch - 1;
   const int row = t0 + threadIdx.x;
   const long long slot = row < p.T ? pw_slot(p, row) : -1;
   __nv_bfloat16* dst = slot >= 0 ? p.cache + (slot / p.page) * p.sblk + (slot % p.page) * p.stok : nullptr;
@@ -160,8 +164,8 @@ __global__ void __launch_bounds__(kPwThreads, 1)
           float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
           if (group) {
             const int c = col0 + 32 * half + 2 * j;
-            if (!in_runs(p, g, c)) lo = 0.f;
-            if (!in_runs(p, g, c + 1)) hi = 0.f;
+            if (!in_runs(c)) lo = 0.f;
+            if (!in_runs(c + 1)) hi = 0.f;
           }
           pk[j] = pack_bf16(lo, hi);
         }
@@ -249,12 +253,15 @@ __global__ void __launch_bounds__(kPwThreads, 1)
       if (dst) {
         const uint8_t* a2 = smem + kPwA2;
         for (int run = 0; run < 2; ++run) {
-          const int lo = run ? p.b_lo[g] : p.a_lo[g], n = run ? p.b_n[g] : p.a_n[g];
+          const int lo = run ? b_lo : a_lo, n = run ? b_hi - b_lo : a_hi - a_lo;
           int c = lo;
           while (c < lo + n) {
-            // window position of column c
-            int i = 0;
-            while (i + 1 < nch && p.item_chunk[item][i] != (c >> 6)) ++i;
+            // window position of column c (the window's chunks ascend; contiguous windows need no search)
+            int i = (c >> 6) - win_lo;
+            if (!win_contig) {
+              i = 0;
+              while (i + 1 < nch && p.item_chunk[item][i] != (c >> 6)) ++i;
+            }
             const int j = c & 63;
             const uint8_t* unit = a2 + i * kPwXBytes + sw128(threadIdx.x, j >> 3);
             if ((c & 7) == 0 && c + 8 <= lo + n && p.vec_ok) {
