@@ -31,6 +31,8 @@ SIGNATURES = {
     "belt_latent_decode_noalloc": [c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp,
                                    c_i32, c_i32, c_f32, c_i32, c_i32, c_i32p, c_vp, c_i32, c_vp, c_i32, c_vp, c_i64,
                                    c_i64, c_vp, c_i64, c_vp, c_vp],
+    "belt_latent_decompress": [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32,
+                               c_i32p, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
     "belt_selftest_bounded_wait": [c_vp, c_vp, c_vp],
     "belt_num_sms": [c_i32],
     "belt_abi_version": [],

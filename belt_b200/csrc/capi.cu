@@ -564,6 +564,94 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
 }
 
+int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                           int64_t stride_block, int64_t stride_tok, const int32_t* block_table_row, int32_t seq_len,
+                           int32_t pos0, int32_t count, const void* wk, int32_t kc, const int32_t* k_segs,
+                           const void* v_up, int32_t v_offset, int32_t r_v, const void* cos_sin, int32_t max_pos,
+                           void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, void* stream) {
+  using namespace belt;
+  if (count < 0 || pos0 < 0 || seq_len < 0 || static_cast<int64_t>(pos0) + count > seq_len)
+    return fail(BELT_ERR_INVALID, "latent_decompress: positions [%d, %d) outside the request's %d", pos0, pos0 + count,
+                seq_len);
+  if (count == 0) return ok();
+  if (!cache || !block_table_row || !wk || !k_segs || !v_up || !cos_sin || !k_out || !v_out)
+    return fail(BELT_ERR_INVALID, "latent_decompress: null buffer");
+  if (!(page == 16 || page == 32 || page == 64 || (page % 128 == 0 && page > 0)))
+    return fail(BELT_ERR_INVALID, "latent_decompress: page size %d (supported: 16, 32, 64 or a multiple of 128)", page);
+  if (num_blocks < 1 || num_blocks > (1ll << 31) - 2 || row_width <= 0 || stride_tok < row_width || stride_tok % 8 ||
+      stride_block % 8 || !aligned16(cache))
+    return fail(BELT_ERR_INVALID, "latent_decompress: cache rows must be 16-byte aligned (strides %lld, %lld)",
+                (long long)stride_block, (long long)stride_tok);
+  if (kc <= 0 || kc % 64 || kc > row_width + 63 || r_v <= 0 || r_v > 1024 || v_offset < 0 || v_offset + r_v > row_width)
+    return fail(BELT_ERR_INVALID, "latent_decompress: kc %d, v_offset %d, r_v %d, row width %d", kc, v_offset, r_v,
+                row_width);
+  if (max_pos < seq_len) return fail(BELT_ERR_INVALID, "latent_decompress: cos_sin has %d rows < %d", max_pos, seq_len);
+  if (!aligned16(wk) || !aligned16(v_up) || !aligned16(k_out) || !aligned16(v_out) || out_st % 8 || out_sg % 8 ||
+      out_sg < 256 || out_st < 4 * out_sg)
+    return fail(BELT_ERR_INVALID, "latent_decompress: weights and outputs 16-byte aligned, output strides");
+  DecompressParams p{};
+  p.block_table = block_table_row;
+  p.seq_len = seq_len;
+  p.page = page;
+  p.num_blocks = static_cast<int>(num_blocks);
+  p.pos0 = pos0;
+  p.count = count;
+  for (int g = 0; g < kG; ++g) {
+    const int runs[2][2] = {{k_segs[4 * g], k_segs[4 * g + 1]}, {k_segs[4 * g + 2], k_segs[4 * g + 3]}};
+    bool use[64] = {};
+    for (int q = 0; q < 2; ++q) {
+      if (runs[q][1] <= 0) continue;
+      if (runs[q][0] < 0 || runs[q][0] + runs[q][1] > kc)
+        return fail(BELT_ERR_INVALID, "latent_decompress: k_segs of group %d outside the key part", g);
+      for (int c = runs[q][0] >> 6; c <= (runs[q][0] + runs[q][1] - 1) >> 6 && c < 64; ++c) use[c] = true;
+    }
+    int n = 0;
+    for (int c = 0; c < 64; ++c)
+      if (use[c]) {
+        if (n == kPwMaxChunks)
+          return fail(BELT_ERR_INVALID, "latent_decompress: group %d spans more than %d 64-column chunks", g,
+                      kPwMaxChunks);
+        p.k_chunk[g][n++] = c;
+      }
+    p.k_nch[g] = n;
+  }
+  p.v_offset = v_offset;
+  p.v_chunk0 = v_offset / 64;
+  p.v_nch = (v_offset + r_v + 63) / 64 - p.v_chunk0;
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+  p.max_pos = max_pos;
+  p.k_out = static_cast<__nv_bfloat16*>(k_out);
+  p.v_out = static_cast<__nv_bfloat16*>(v_out);
+  p.out_st = out_st;
+  p.out_sg = out_sg;
+  p.err = err;
+  DecompressMaps maps;
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_width), static_cast<cuuint64_t>(page),
+                          static_cast<cuuint64_t>(num_blocks)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_tok) * 2, static_cast<cuuint64_t>(stride_block) * 2};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(page < 128 ? page : 128), 1};
+    int r = encode_bf16(&maps.cache, cache, 3, dims, strides, box, "cache");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kc), 256, static_cast<cuuint64_t>(kG)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kc) * 2, static_cast<cuuint64_t>(kc) * 256 * 2};
+    cuuint32_t box[3] = {64, 256, 1};
+    int r = encode_bf16(&maps.wk, wk, 3, dims, strides, box, "wk");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[3] = {256, static_cast<cuuint64_t>(r_v), static_cast<cuuint64_t>(kG)};
+    cuuint64_t strides[2] = {256 * 2, static_cast<cuuint64_t>(r_v) * 256 * 2};
+    cuuint32_t box[3] = {64, 64, 1};
+    int r = encode_bf16(&maps.v, v_up, 3, dims, strides, box, "v_up");
+    if (r != BELT_OK) return r;
+  }
+  cudaError_t e = launch_decompress(maps, p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decompress launch");
+}
+
 int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream) {
   if (!err || !status) return fail(BELT_ERR_INVALID, "selftest_bounded_wait: null buffer");
   cudaError_t e = belt::launch_selftest_wait(err, status, as_stream(stream));

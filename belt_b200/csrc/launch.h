@@ -162,6 +162,28 @@ struct ProjWriteParams {
 };
 cudaError_t launch_proj_write(const ProjWriteMaps& maps, const ProjWriteParams& p, cudaStream_t stream);
 
+// Keys and values of cached positions rebuilt from the latent rows (decompress.cu).
+struct DecompressMaps {
+  CUtensorMap cache;   // {W, page, blocks}, box {64, min(page, 128), 1}
+  CUtensorMap wk;      // [4, 256, kc] key weights, box {64, 256, 1}
+  CUtensorMap v;       // v_up [4, r_v, 256], box {64, 64, 1}
+};
+struct DecompressParams {
+  const int32_t* block_table;   // the request's row
+  int seq_len, page, num_blocks;
+  int pos0, count;
+  int k_nch[4];
+  int k_chunk[4][kPwMaxChunks];
+  int v_chunk0, v_nch, v_offset;
+  const __nv_bfloat16* cos_sin;
+  int max_pos;
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;
+  long long out_st, out_sg;
+  int* err;
+};
+cudaError_t launch_decompress(const DecompressMaps& maps, const DecompressParams& p, cudaStream_t stream);
+
 // Bounded-wait self-test (selftest.cu).
 cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);
 

@@ -8,7 +8,9 @@
 * ``latent_rows_to_cache``: the per-token cache rows ``[c_K / rho | 0 | c_v | 0]`` into the paged KV cache
   (latent_ops.py:138-158);
 * ``project_rows_to_cache``: the same rows computed from the layer inputs, the model's ``kv_latent_proj`` linear
-  (models/qwen3_5_latent.py:139-140, 213) fused into the write on the tensor cores.
+  (models/qwen3_5_latent.py:139-140, 213) fused into the write on the tensor cores;
+* ``decompress_paged``: keys and values of a request's cached positions rebuilt from its latent rows (the prefill
+  path's ``LatentLayer.decompress``, latent_backend.py:95-108) on the tensor cores.
 """
 
 from __future__ import annotations
@@ -132,3 +134,37 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
               w_down.stride(0), slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), cache.data_ptr(),
               cache.shape[0], cache.shape[1], W, cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk,
               _lib.int_array(segs), float(eps), error_word(x.device).data_ptr(), _stream_ptr(x.device))
+
+
+def decompress_paged(cache: torch.Tensor, block_table_row: torch.Tensor, seq_len: int, pos0: int, count: int,
+                     wk: torch.Tensor, k_segs, v_up_t: torch.Tensor, v_offset: int, cos_sin: torch.Tensor,
+                     k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None):
+    """Keys and values [count, G, D] BF16 of positions [pos0, pos0 + count) of one request, rebuilt from its latent rows
+    in ``cache`` [blocks, page, W] (rows gathered through ``block_table_row``) on the tensor cores: the reference's
+    ``LatentLayer.decompress`` (latent_backend.py:95-108) of the gathered rows (latent_backend.py:214-225). ``wk``
+    [G, D, n_k * 64]: per group the rope rows of U_g times the gain, then the nope rows of qmap (``LatentLayer.wk``)."""
+    G, D, kc = wk.shape
+    r_v = v_up_t.shape[1]
+    dev = cache.device
+    if k_out is None:
+        k_out = torch.empty(count, G, D, dtype=torch.bfloat16, device=dev)
+    if v_out is None:
+        v_out = torch.empty(count, G, D, dtype=torch.bfloat16, device=dev)
+    if count == 0:
+        return k_out, v_out
+    if cache.dtype != torch.bfloat16 or cache.stride(-1) != 1 or block_table_row.dtype != torch.int32:
+        raise ValueError("decompress_paged: BF16 cache with contiguous rows, int32 block table")
+    if G != 4 or D != HEAD_DIM or not wk.is_contiguous() or not v_up_t.is_contiguous() or v_up_t.shape[0] != G:
+        raise ValueError("decompress_paged: wk [4, 256, kc] and v_up [4, r_v, 256] contiguous")
+    for name, t in (("k_out", k_out), ("v_out", v_out)):
+        if t.dtype != torch.bfloat16 or tuple(t.shape) != (count, G, D) or t.stride(2) != 1:
+            raise ValueError(f"decompress_paged: {name} [count, 4, 256] BF16 with contiguous channels")
+    if k_out.stride() != v_out.stride():
+        raise ValueError("decompress_paged: k_out and v_out with the same strides")
+    from .decode import error_word
+    _lib.call("belt_latent_decompress", cache.data_ptr(), cache.shape[0], cache.shape[1], cache.shape[2],
+              cache.stride(0), cache.stride(1), block_table_row.data_ptr(), int(seq_len), int(pos0), int(count),
+              wk.data_ptr(), kc, _lib.int_array(host_k_segs(k_segs)), v_up_t.data_ptr(), int(v_offset), r_v,
+              cos_sin.data_ptr(), cos_sin.shape[0], k_out.data_ptr(), v_out.data_ptr(), k_out.stride(0),
+              k_out.stride(1), error_word(dev).data_ptr(), _stream_ptr(dev))
+    return k_out, v_out

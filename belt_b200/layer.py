@@ -41,6 +41,7 @@ class LatentLayer:
     rope: RopeRebuild = None    # RoPE keys rebuilt in-kernel from the K latent
     rope_up: torch.Tensor = None  # [G, rot, n_k * 64] gain * rotary rows of U_g by column
     k_segs_host: list = field(default_factory=list)   # k_segs as host ints (no device sync on the hot path)
+    wk: torch.Tensor = None     # [G, D, n_k * 64]: per group rope_up then qmap's nope rows (the keys of decompress)
 
     @property
     def col_runs(self) -> list:
@@ -53,6 +54,14 @@ class LatentLayer:
     def up_project(self, a: torch.Tensor, out: torch.Tensor) -> None:
         """[T, H, r_v] latent-space attention output -> out [T, H, head_dim] (latent_backend.py:91-93)."""
         latent_ops.up_project(a, self.v_up, out)
+
+    def decompress_paged(self, cache: torch.Tensor, block_table_row: torch.Tensor, seq_len: int, pos0: int,
+                         count: int, k_out=None, v_out=None):
+        """Keys and values [count, G, D] of positions [pos0, pos0 + count) of one request, rebuilt on the tensor cores
+        from its rows in ``cache`` [blocks, page, W] (``latent_ops.decompress_paged``): ``decompress`` of the gathered
+        rows in one kernel."""
+        return latent_ops.decompress_paged(cache, block_table_row, seq_len, pos0, count, self.wk, self.k_segs_host,
+                                           self.v_up, self.v_offset, self.rope.cos_sin, k_out, v_out)
 
     def decompress(self, rows: torch.Tensor, positions: torch.Tensor):
         """Cached rows [S, row_width] at text positions [S] -> the model's keys and values [S, G, head_dim] (RoPE
@@ -112,6 +121,7 @@ def derive_latent_tensors(k_up: torch.Tensor, v_up: torch.Tensor, k_norm_weight:
     for g, ((off, rr), u) in enumerate(zip(groups, u_rot)):
         rope_up[g, :, off:off + rr] = u.to(dtype)
     rows = k_segs_rows(layout)
+    wk = torch.cat([rope_up, qmap[:, rot:, :n_k * CHUNK].to(dtype)], dim=1).contiguous()
     v_up_t = v_up.view(G, D, r_v).transpose(1, 2).contiguous()
     cos_sin = cos_sin_cache.detach().to("cpu").to(torch.bfloat16).contiguous()
     to = dict(device=device)
@@ -121,4 +131,4 @@ def derive_latent_tensors(k_up: torch.Tensor, v_up: torch.Tensor, k_norm_weight:
                        k_segs=torch.tensor(rows, dtype=torch.int32, **to), rope_gain=gain[:rot].clone().to(**to),
                        eps=float(eps), rotary=rotary, mrope_section=mrope_section,
                        rope=RopeRebuild(groups=groups, blocks=blocks.to(**to), cos_sin=cos_sin.to(**to)),
-                       rope_up=rope_up.to(**to), k_segs_host=rows)
+                       rope_up=rope_up.to(**to), k_segs_host=rows, wk=wk.to(**to))

@@ -163,6 +163,22 @@ int belt_latent_decode_noalloc(const void* q_bd, int32_t num_reqs, int32_t kq, c
                                float* lse, int64_t lse_sb, int32_t* err, void* stream);
 
 /*
+ * Keys and values of cached positions [pos0, pos0 + count) of one request, rebuilt from its latent rows: replaces
+ * latent_backend.py:95-108 (`LatentLayer.decompress`) applied to rows gathered through the request's block table
+ * (latent_backend.py:214-225), the prefill path's input to its attention.
+ *   cache [num_blocks, page, W] BF16 view as belt_latent_decode; block_table_row [>= ceil(seq_len / page)] int32;
+ *   wk [4, 256, kc] BF16 contiguous: per group [rope_up[g]; qmap[g, 64:, :kc]], kc = n_k * 64;
+ *   k_segs host int32 [4][4] (the groups' column runs); v_up [4, r_v, 256] BF16 contiguous; cos_sin [max_pos, 64];
+ *   k_out, v_out [count, 4, 256] BF16 views with element strides (out_st, out_sg, 1): k = [RoPE(bf16(x)) | k_nope].
+ * Rounding as the reference: BF16 products of the matmuls, the rotation in fp32, BF16 out.
+ */
+int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                           int64_t stride_block, int64_t stride_tok, const int32_t* block_table_row, int32_t seq_len,
+                           int32_t pos0, int32_t count, const void* wk, int32_t kc, const int32_t* k_segs,
+                           const void* v_up, int32_t v_offset, int32_t r_v, const void* cos_sin, int32_t max_pos,
+                           void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, void* stream);
+
+/*
  * Self-test of the kernels' bounded waits (no counterpart in the reference): launches one thread that waits on a
  * barrier nothing completes. The wait gives up after the same limit the decode kernel uses (~2 s), writes 0x1F0 into
  * the device word `err` (if still 0), and the kernel ends normally; status (device int32[2]) receives {2, 1} (wait gave

@@ -476,3 +476,57 @@ def test_decode_config4_long_context(spec_name):
     assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS
     alone, *_ = run_decode(lat, q[30:31], cache, bt[30:31].to(DEV), sl[30:31])
     assert float((alone.float() - out[30:31].float()).abs().max()) < MAX_ABS
+
+
+# ------------------------------------------------------------------------------------------------- decompress (prefill)
+def assert_decompress_close(k, v, ek, ev, what):
+    """Values and the keys' non-rotary channels within 1 BF16 ulp. The rotary channels are x1 cos - x2 sin (and
+    x2 cos + x1 sin) of x = bf16(gain B_g c~): a sum order that moves x by one BF16 ulp moves the rotated value by up
+    to one ulp of |x| (2^-8 |x|), so they are held to 2^-7 (1 + |expected|) absolute, and almost all within 1 ulp."""
+    assert bf16_ulp_close(v, ev, ulps=1, atol=1e-6), (what, "v")
+    assert bf16_ulp_close(k[..., 64:], ek[..., 64:], ulps=1, atol=1e-6), (what, "k nope")
+    kp, ep = k[..., :64].float(), ek[..., :64].float()
+    assert ((kp - ep).abs() <= 2 ** -7 * (1 + ep.abs())).all(), (what, "k rope", float((kp - ep).abs().max()))
+    mag = torch.maximum(kp.abs(), ep.abs()).clamp_min(1e-38)
+    far = (kp - ep).abs() > 2.0 ** (torch.floor(torch.log2(mag)) - 7) + 1e-6
+    assert float(far.float().mean()) < 1e-4, (what, "k rope beyond 1 ulp", float(far.float().mean()))
+
+
+@pytest.mark.parametrize("r_k", [384, 448, 512, 640])
+@pytest.mark.parametrize("page", [16, 64, 128])
+def test_decompress_paged(r_k, page):
+    """Keys and values of position ranges rebuilt from the paged rows on the tensor cores, against the oracle's
+    ``decompress`` of the gathered rows: whole requests, ranges that start and end inside a 128-position tile and a
+    page, and a single position. Every channel within 1 BF16 ulp (the rotation's and the sums' rounding order)."""
+    spec = synth.spec_from_ranks(r_k, 1024 - r_k)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=3000)
+    seqs = [2049, 1, 700, 129]
+    batch = synth.make_batch(w.layout, seqs, page=page, seed=31)
+    cache, bt = batch.cache.to(DEV), batch.block_table.to(DEV)
+    for b, (pos0, count) in [(0, (0, 2049)), (1, (0, 1)), (2, (37, 600)), (3, (128, 1)), (2, (699, 1)),
+                             (0, (1000, 777))]:
+        L = seqs[b]
+        k, v = lat.decompress_paged(cache, bt[b], L, pos0, count)
+        torch.cuda.synchronize()
+        dec.check_device_errors(DEV)
+        rows, pos = oracle.gather_rows(batch.cache, batch.block_table, b, L)
+        ek, ev = oracle.decompress(ref, rows[pos0:pos0 + count], pos[pos0:pos0 + count])
+        assert_decompress_close(k.cpu(), v.cpu(), ek, ev, (r_k, page, b, pos0, count))
+
+
+def test_decompress_into_strided_views():
+    """Outputs written into views of a larger buffer ([count, 4, 256] slices with a token stride of 2 * 1024): the
+    neighbouring halves stay untouched."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=1200)
+    seqs = [1100]
+    batch = synth.make_batch(w.layout, seqs, page=16, seed=32)
+    buf = torch.zeros(300, 2, 4, 256, dtype=torch.bfloat16, device=DEV)
+    k_out, v_out = buf[:, 0], buf[:, 1]
+    lat.decompress_paged(batch.cache.to(DEV), batch.block_table.to(DEV)[0], 1100, 500, 300, k_out, v_out)
+    torch.cuda.synchronize()
+    rows, pos = oracle.gather_rows(batch.cache, batch.block_table, 0, 1100)
+    ek, ev = oracle.decompress(ref, rows[500:800], pos[500:800])
+    assert_decompress_close(buf[:, 0].cpu(), buf[:, 1].cpu(), ek, ev, "strided views")
