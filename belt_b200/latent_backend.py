@@ -256,8 +256,8 @@ class LatentAttentionImpl:
 
     def _prefill(self, lat: LatentLayer, query: torch.Tensor, output: torch.Tensor, cache: torch.Tensor,
                  m: LatentAttentionMetadata) -> None:
-        """Each prefill request's new tokens over its whole context (causal), keys and values decompressed from the
-        cache rows in chunks of ``PREFILL_CHUNK`` context tokens merged by log-sum-exp."""
+        """Each prefill request's new tokens over its whole context (causal), keys and values rebuilt from the cache rows
+        (``LatentLayer.decompress_paged``) in chunks of ``PREFILL_CHUNK`` context tokens merged by log-sum-exp."""
         nd, page = m.num_decodes, cache.shape[1]
         hpg = self.num_heads // lat.num_kv_heads
         tok = m.num_decode_tokens
@@ -272,8 +272,8 @@ class LatentAttentionImpl:
             for c0 in range(0, L, step):
                 c1 = min(L, c0 + step)
                 pos = torch.arange(c0, c1, device=query.device)
-                rows = cache[m.block_table[b, pos // page].long(), pos % page]
-                k, v = lat.decompress(rows, pos)
+                # keys and values of the chunk rebuilt from the paged rows on the tensor cores
+                k, v = lat.decompress_paged(cache, m.block_table[b], L, c0, c1 - c0)
                 k = k.transpose(0, 1).repeat_interleave(hpg, dim=0).float()   # [H, S, D]
                 v = v.transpose(0, 1).repeat_interleave(hpg, dim=0).float()
                 s = torch.einsum("hqd,hsd->hqs", q.float(), k) * self.scale

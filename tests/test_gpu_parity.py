@@ -530,3 +530,54 @@ def test_decompress_into_strided_views():
     rows, pos = oracle.gather_rows(batch.cache, batch.block_table, 0, 1100)
     ek, ev = oracle.decompress(ref, rows[500:800], pos[500:800])
     assert_decompress_close(buf[:, 0].cpu(), buf[:, 1].cpu(), ek, ev, "strided views")
+
+
+def test_backend_forward_mixed_prefill():
+    """Decodes and prefills in one step through the backend: every new token's row written, the decodes through the
+    split-KV kernel, the prefills' queries (several per request, the last positions of their contexts) attending
+    causally over keys and values rebuilt on the tensor cores, against the fp32 oracle (decompress + attention)."""
+    spec = synth.spec_from_ranks(448, 576)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=2100)
+    seqs = [300, 1, 129, 700, 2050]          # the last two are prefills of 37 and 300 new tokens
+    qlens = [1, 1, 1, 37, 300]
+    page = 16
+    bt, nb, _ = synth.block_tables(seqs, page, extra_blocks=2)
+    W = w.layout["row_width"]
+    kv = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv[:, 0], w.layout, bt, seqs, seed=4, poison=False)
+    B, T = len(seqs), sum(qlens)
+    g = torch.Generator().manual_seed(14)
+    c = torch.randn(T, W, generator=g).to(torch.bfloat16)                     # the new tokens' latent projections
+    pos = torch.cat([torch.arange(L - ql, L) for L, ql in zip(seqs, qlens)])
+    req = torch.cat([torch.full((ql,), b) for b, ql in enumerate(qlens)])
+    slots = bt[req, pos // page].long() * page + pos % page
+    q = torch.randn(T, 24, 256, generator=g).to(torch.bfloat16)
+    exp_cache = oracle.latent_rows(c, slots, kv[:, 0].clone(), ref["u_cat"], ref["k_segs"], 1e-6)
+    exp = torch.zeros(T, 24, 256)
+    for t in range(T):
+        b, p = int(req[t]), int(pos[t])
+        rows, rpos = oracle.gather_rows(exp_cache, bt, b, p + 1)
+        k, v = oracle.decompress(ref, rows, rpos)
+        exp[t] = oracle.attend(q[t], k, v, SCALE)
+
+    spec_kv = LatentKVSpec(block_size=page, num_kv_heads=1, head_size=W)
+    builder = LatentAttentionMetadataBuilder(spec_kv, ["l0"], device=DEV, max_num_batched_tokens=512)
+    qsl = torch.tensor([0] + list(torch.cumsum(torch.tensor(qlens), 0)), dtype=torch.int32)
+    cm = CommonAttentionMetadata(query_start_loc=qsl.to(DEV), query_start_loc_cpu=qsl,
+                                 seq_lens=torch.tensor(seqs, dtype=torch.int32, device=DEV),
+                                 block_table_tensor=bt.to(DEV), slot_mapping=slots.to(DEV), num_reqs=B,
+                                 num_actual_tokens=T, max_query_len=max(qlens))
+    md = builder.build(0, cm)
+    assert md.num_decodes == 3 and md.num_prefills == 2
+    impl = LatentAttentionImpl(24, 256, SCALE, 4)
+
+    class Layer:
+        latent = lat
+    kv_d = kv.to(DEV)
+    output = torch.empty(T, 24, 256, dtype=torch.bfloat16, device=DEV)
+    impl.forward(Layer, q.to(DEV), c.to(DEV), pos.to(DEV), kv_d, md, output)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    assert bf16_ulp_close(kv_d[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=1)
+    assert_close_out(output, exp, "mixed prefill")
