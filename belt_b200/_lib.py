@@ -33,6 +33,8 @@ SIGNATURES = {
                                    c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_latent_decompress": [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32,
                                c_i32p, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
+    "belt_prefill_attention": [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_f32,
+                               c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_selftest_bounded_wait": [c_vp, c_vp, c_vp],
     "belt_num_sms": [c_i32],
     "belt_abi_version": [],

@@ -652,6 +652,57 @@ int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, 
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decompress launch");
 }
 
+int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh, const void* k, const void* v,
+                           int32_t num_keys, int64_t kv_st, int64_t kv_sg, int32_t q_pos0, int32_t k_pos0,
+                           int32_t causal, float scale, void* out, int64_t out_st, int64_t out_sh, float* lse,
+                           int64_t lse_st, int32_t* err, void* stream) {
+  using namespace belt;
+  if (ql < 0 || num_keys < 0) return fail(BELT_ERR_INVALID, "prefill_attention: ql %d, keys %d", ql, num_keys);
+  if (ql == 0) return ok();
+  if (!q || !out || (num_keys > 0 && (!k || !v)))
+    return fail(BELT_ERR_INVALID, "prefill_attention: null buffer");
+  if (!aligned16(q) || !aligned16(out) || (num_keys > 0 && (!aligned16(k) || !aligned16(v))) || q_st % 8 ||
+      q_sh % 8 || kv_st % 8 || kv_sg % 8 || out_st % 8 || out_sh % 8 || q_sh < 256 || q_st < kH * q_sh ||
+      kv_sg < 256 || kv_st < kG * kv_sg || out_sh < 256 || out_st < kH * out_sh)
+    return fail(BELT_ERR_INVALID, "prefill_attention: 16-byte aligned tensors, strides multiples of 8 elements");
+  if (lse && lse_st < kH) return fail(BELT_ERR_INVALID, "prefill_attention: lse row stride %lld", (long long)lse_st);
+  PrefillAttnParams p{};
+  p.ql = ql;
+  p.S = num_keys;
+  p.H = kH;
+  p.hpg = kHPG;
+  p.q_pos0 = q_pos0;
+  p.k_pos0 = k_pos0;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_st = out_st;
+  p.out_sh = out_sh;
+  p.lse = lse;
+  p.lse_st = lse_st;
+  p.err = err;
+  PrefillAttnMaps maps;
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kH), static_cast<cuuint64_t>(ql)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(q_sh) * 2, static_cast<cuuint64_t>(q_st) * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    int r = encode_bf16(&maps.q, q, 3, dims, strides, box, "q");
+    if (r != BELT_OK) return r;
+  }
+  const int nk = num_keys > 0 ? num_keys : 1;   // a map of one row when there are no keys (never read)
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kG), static_cast<cuuint64_t>(nk)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kv_sg) * 2, static_cast<cuuint64_t>(kv_st) * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    int r = encode_bf16(&maps.k, num_keys > 0 ? k : q, 3, dims, strides, box, "k");
+    if (r != BELT_OK) return r;
+    r = encode_bf16(&maps.v, num_keys > 0 ? v : q, 3, dims, strides, box, "v");
+    if (r != BELT_OK) return r;
+  }
+  cudaError_t e = launch_prefill_attn(maps, p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "prefill_attention launch");
+}
+
 int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream) {
   if (!err || !status) return fail(BELT_ERR_INVALID, "selftest_bounded_wait: null buffer");
   cudaError_t e = belt::launch_selftest_wait(err, status, as_stream(stream));

@@ -184,6 +184,24 @@ struct DecompressParams {
 };
 cudaError_t launch_decompress(const DecompressMaps& maps, const DecompressParams& p, cudaStream_t stream);
 
+// Prefill attention (prefill_attn.cu).
+struct PrefillAttnMaps {
+  CUtensorMap q;   // [ql, H, 256], box {64, 1, 128}
+  CUtensorMap k;   // [S, G, 256], box {64, 1, 128}
+  CUtensorMap v;
+};
+struct PrefillAttnParams {
+  int ql, S, H, hpg;
+  int q_pos0, k_pos0, causal;
+  float scale_log2;
+  __nv_bfloat16* out;
+  long long out_st, out_sh;
+  float* lse;          // [ql, H] (row stride lse_st), may be null
+  long long lse_st;
+  int* err;
+};
+cudaError_t launch_prefill_attn(const PrefillAttnMaps& maps, const PrefillAttnParams& p, cudaStream_t stream);
+
 // Bounded-wait self-test (selftest.cu).
 cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);
 

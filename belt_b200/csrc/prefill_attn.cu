@@ -1,0 +1,280 @@
+// Prefill attention on the tensor cores: the new tokens of one request attend over keys and values rebuilt from its
+// cache rows (belt_latent_decompress), the operation the reference hands to flash_attn_varlen_func
+// (plugins/vllm_lrkv/vllm_lrkv/latent_backend.py:285-320): softmax(scale q k^T) v per query head, heads sharing
+// their group's keys (24 query heads, 4 groups, head dim 256), causal by position, with the natural-log LSE of every
+// (query, head) so that the backend can fold context chunks together.
+//
+// One CTA per (128-query tile, head), 192 threads:
+//   * warp 0, lane 0: TMA producer. The query tile (128 x 256, K-major, 4 chunks of 64 columns, 128-byte swizzle)
+//     once; per 128-key tile the keys (same layout) and the values (read as the MN-major B operand: 128 key rows of
+//     64 channels per block, four blocks), each into its own single buffer;
+//   * warp 1, lane 0: tcgen05 issuer. S = Q K^T (M = 128 queries, N = 128 keys, 16 steps of K = 16) into TMEM,
+//     then O += P V with P read from TMEM (M = 128, N = 256, 8 steps), software-pipelined: S of tile j + 1 is computed
+//     while the softmax turns S of tile j into P;
+//   * warps 2-5: softmax, one query row per thread (its TMEM lane): scale, mask (keys past the end or, causally,
+//     after the query's position), running max in the exp2 domain (O rescaled in TMEM only when a row's max grows by
+//     more than 2^8), P = exp2(s - m) packed to BF16 into TMEM, row sums in fp32; at the end O / l to BF16 and the
+//     LSE.
+// TMEM: S [0, 128), P [128, 192) (BF16 pairs), O [256, 512).
+// Every wait is bounded: a timeout records an error code and the CTA drains its copies and exits.
+#include "common.cuh"
+#include "launch.h"
+
+namespace belt {
+
+namespace {
+constexpr int kPaThreads = 192;
+constexpr int kPaTile = 128;
+constexpr int kPaChunk = 128 * 128;             // 128 rows x 64 channels (BF16), one swizzled chunk
+constexpr int kPaTileBytes = 4 * kPaChunk;      // 128 x 256 = 64 KB
+constexpr int kPaQ = 0, kPaK = kPaTileBytes, kPaV = 2 * kPaTileBytes;
+constexpr int kPaSmem = 3 * kPaTileBytes;       // + barriers
+constexpr uint32_t kTmS = 0, kTmP = 128, kTmO = 256;
+// barriers
+constexpr int aQ = 0, aKFull = 1, aKEmpty = 2, aVFull = 3, aVEmpty = 4, aSFull = 5, aSFree = 6, aPFull = 7,
+              aPvDone = 8, aDrain = 9, kPaBars = 10;
+}  // namespace
+
+__global__ void __launch_bounds__(kPaThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ PrefillAttnMaps maps, const __grid_constant__ PrefillAttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPaSmem);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kPaBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i0 = blockIdx.x * kPaTile, h = blockIdx.y, g = h / p.hpg;
+  const int q_last = min(i0 + kPaTile, p.ql) - 1;   // last live query of the tile
+  // key tiles to visit: all of them, or causally those holding a key at or before the tile's last query position
+  int n_tiles = (p.S + kPaTile - 1) / kPaTile;
+  if (p.causal) {
+    const long long last_key = static_cast<long long>(p.q_pos0) + q_last - p.k_pos0;   // last key index allowed
+    const long long lim = last_key < 0 ? 0 : last_key / kPaTile + 1;
+    n_tiles = static_cast<int>(lim < n_tiles ? lim : n_tiles);
+  }
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPaBars; ++i) mbar_init(&bars[i], (i == aSFree || i == aPFull) ? 4 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&maps.q);
+    tma_prefetch_desc(&maps.k);
+    tma_prefetch_desc(&maps.v);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0 && n_tiles > 0) {
+      int k_issued = 0, v_issued = 0;
+      mbar_arrive_expect_tx(&bars[aQ], kPaTileBytes);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tma_load_3d(smem + kPaQ + c * kPaChunk, &maps.q, &bars[aQ], 64 * c, h, i0);
+      for (int j = 0; j < n_tiles; ++j) {
+        if (j > 0 && !mbar_wait(&bars[aKEmpty], (j - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&bars[aKFull], kPaTileBytes);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_3d(smem + kPaK + c * kPaChunk, &maps.k, &bars[aKFull], 64 * c, g, j * kPaTile);
+        ++k_issued;
+        if (j > 0 && !mbar_wait(&bars[aVEmpty], (j - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&bars[aVFull], kPaTileBytes);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tma_load_3d(smem + kPaV + c * kPaChunk, &maps.v, &bars[aVFull], 64 * c, g, j * kPaTile);
+        ++v_issued;
+      }
+      if (*abort_flag) {
+        // the latest copy into every buffer lands before the CTA's shared memory goes away
+        mbar_wait_bounded(&bars[aQ], 0, nullptr, 0, kWaitCycles / 8);
+        if (k_issued) mbar_wait_bounded(&bars[aKFull], (k_issued - 1) & 1, nullptr, 0, kWaitCycles / 8);
+        if (v_issued) mbar_wait_bounded(&bars[aVFull], (v_issued - 1) & 1, nullptr, 0, kWaitCycles / 8);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- tcgen05 issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);   // Q K-major, K K-major
+      constexpr uint32_t idO = idesc_bf16(128, 256, 0, 1);   // P from TMEM, V MN-major
+      constexpr uint32_t hiSw = desc_hi(1024, kSwizzle128);
+      const uint32_t base = smem_u32(smem);
+      bool ok = true;
+      auto wait = [&](int bar, uint32_t parity) -> bool {
+        return mbar_wait(&bars[bar], parity, abort_flag, p.err, kErrTimeoutMma);
+      };
+      auto qk = [&](int j) -> bool {
+        if (!wait(aKFull, j & 1)) return false;
+        if (j > 0 && !wait(aSFree, (j - 1) & 1)) return false;   // the softmax has read S of the previous tile
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          const uint32_t off = (s >> 2) * kPaChunk + (s & 3) * 32;
+          mma_ss(tmem + kTmS, desc_of(desc_lo(base + kPaQ + off, 16), hiSw),
+                 desc_of(desc_lo(base + kPaK + off, 16), hiSw), idS, s ? 1u : 0u);
+        }
+        mma_commit(&bars[aKEmpty]);
+        mma_commit(&bars[aSFull]);
+        return true;
+      };
+      auto pv = [&](int j) -> bool {
+        if (!wait(aVFull, j & 1)) return false;
+        if (!wait(aPFull, j & 1)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          // A = P (TMEM, 16 keys = 8 columns per step), B = V: 16 key rows = 2 KB per step, 64-channel blocks 16 KB
+          mma_ts(tmem + kTmO, tmem + kTmP + 8 * s, desc_of(desc_lo(base + kPaV + s * 2048, kPaChunk), hiSw), idO,
+                 (j | s) ? 1u : 0u);
+        mma_commit(&bars[aVEmpty]);
+        mma_commit(&bars[aPvDone]);
+        return true;
+      };
+      ok = wait(aQ, 0) && qk(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !(ok = qk(j + 1))) break;
+        if (!(ok = pv(j))) break;
+      }
+      if (*abort_flag) {   // the MMAs issued complete before TMEM is freed
+        mma_commit(&bars[aDrain]);
+        mbar_wait_bounded(&bars[aDrain], 0, nullptr, 0, kWaitCycles / 8);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax warps (rows of TMEM lane quadrant)
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int qi = i0 + row;
+    const bool live_row = qi < p.ql;
+    const long long qpos = static_cast<long long>(p.q_pos0) + qi;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    auto ewait = [&](int bar, uint32_t parity) -> bool {
+      const bool r = mbar_wait(&bars[bar], parity, abort_flag, p.err, kErrTimeoutEpilogue);
+      return __all_sync(0xffffffffu, r);
+    };
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!(ok = ewait(aSFull, j & 1))) break;
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + kTmS + 32 * c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[32 * c + e] = __uint_as_float(r[e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[aSFree]);
+      // scale into the exp2 domain and mask
+      const int k0 = j * kPaTile;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 128; ++e) {
+        const int kj = k0 + e;
+        const bool valid = live_row && kj < p.S && (!p.causal || static_cast<long long>(p.k_pos0) + kj <= qpos);
+        s[e] = valid ? s[e] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[e]);
+      }
+      // the previous tile's P.V has read P and written O: P can be overwritten, O rescaled
+      if (j > 0 && !(ok = ewait(aPvDone, (j - 1) & 1))) break;
+      tc_fence_after();
+      // lazy rescale: a row's running max is raised only when the tile's max exceeds it by more than 2^8; the O
+      // rescale (TMEM loads and stores, warp-collective) runs when any row of the warp needs it, alpha 1 elsewhere
+      float alpha = 1.f;
+      if (mx > m_run + 8.f) {
+        alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - mx);
+        m_run = mx;
+        l_run *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + kTmO + 32 * c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tmem + lane_base + kTmO + 32 * c, o);
+        }
+        tmem_st_wait();
+      }
+      uint32_t pk0[32], pk1[32];
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const float a = m_run == -INFINITY ? 0.f : exp2f(s[2 * e] - m_run);
+        const float b = m_run == -INFINITY ? 0.f : exp2f(s[2 * e + 1] - m_run);
+        sum += a + b;
+        if (e < 32) pk0[e] = pack_bf16(a, b);
+        else pk1[e - 32] = pack_bf16(a, b);
+      }
+      l_run += sum;
+      tmem_st32(tmem + lane_base + kTmP, pk0);
+      tmem_st32(tmem + lane_base + kTmP + 32, pk1);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[aPFull]);
+    }
+    // ---------------------------------------------------------------- epilogue: O / l, LSE
+    if (ok && n_tiles > 0) ok = ewait(aPvDone, (n_tiles - 1) & 1);
+    tc_fence_after();
+    if (ok && !*abort_flag) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __nv_bfloat16* out = p.out + static_cast<long long>(qi) * p.out_st + static_cast<long long>(h) * p.out_sh;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t o[32];
+        if (n_tiles > 0) {
+          tmem_ld32(tmem + lane_base + kTmO + 32 * c, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (!live_row) continue;
+        uint4* dst = reinterpret_cast<uint4*>(out + 32 * c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_bf16(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+      }
+      if (live_row && p.lse)
+        p.lse[static_cast<long long>(qi) * p.lse_st + h] =
+            l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994530942f : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+int prefill_attn_smem_bytes() { return 1024 + kPaSmem + kPaBars * 8 + 16; }
+
+cudaError_t launch_prefill_attn(const PrefillAttnMaps& maps, const PrefillAttnParams& p, cudaStream_t stream) {
+  if (p.ql == 0) return cudaSuccess;
+  const int smem = prefill_attn_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.ql + kPaTile - 1) / kPaTile, p.H);
+  prefill_attn_kernel<<<grid, kPaThreads, smem, stream>>>(maps, p);
+  return cudaGetLastError();
+}
+
+}  // namespace belt

@@ -10,7 +10,9 @@
 * ``project_rows_to_cache``: the same rows computed from the layer inputs, the model's ``kv_latent_proj`` linear
   (models/qwen3_5_latent.py:139-140, 213) fused into the write on the tensor cores;
 * ``decompress_paged``: keys and values of a request's cached positions rebuilt from its latent rows (the prefill
-  path's ``LatentLayer.decompress``, latent_backend.py:95-108) on the tensor cores.
+  path's ``LatentLayer.decompress``, latent_backend.py:95-108) on the tensor cores;
+* ``prefill_attention``: a request's new tokens over those keys and values (causal, with the LSE), the attention of
+  the reference's prefill path (latent_backend.py:285-320).
 """
 
 from __future__ import annotations
@@ -168,3 +170,33 @@ def decompress_paged(cache: torch.Tensor, block_table_row: torch.Tensor, seq_len
               cos_sin.data_ptr(), cos_sin.shape[0], k_out.data_ptr(), v_out.data_ptr(), k_out.stride(0),
               k_out.stride(1), error_word(dev).data_ptr(), _stream_ptr(dev))
     return k_out, v_out
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos0: int, k_pos0: int, scale: float,
+                      causal: bool = True, out: torch.Tensor | None = None, lse: torch.Tensor | None = None):
+    """softmax(scale q k^T) v on the tensor cores for one request's new tokens: q [ql, 24, 256] BF16 at positions
+    q_pos0.., k / v [S, 4, 256] BF16 at positions k_pos0.. (head h reads group h // 6), causal by position. Returns
+    (out [ql, 24, 256] BF16, lse [ql, 24] fp32, natural log; -inf where a query sees no key). The operation of the
+    reference's flash_attn_varlen_func call in its prefill path (latent_backend.py:285-320)."""
+    ql, H, D = q.shape
+    S = k.shape[0]
+    dev = q.device
+    if out is None:
+        out = torch.empty(ql, H, D, dtype=torch.bfloat16, device=dev)
+    if lse is None:
+        lse = torch.empty(ql, H, dtype=torch.float32, device=dev)
+    if ql == 0:
+        return out, lse
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1:
+            raise ValueError(f"prefill_attention: {name} [n, heads, 256] BF16 with contiguous channels")
+    if H != 24 or k.shape[1] != 4 or k.shape != v.shape or k.stride() != v.stride() or tuple(out.shape) != (ql, H, D):
+        raise ValueError("prefill_attention: q [ql, 24, 256], k / v [S, 4, 256] with equal strides, out like q")
+    if lse.dtype != torch.float32 or tuple(lse.shape) != (ql, H) or lse.stride(1) != 1:
+        raise ValueError("prefill_attention: lse [ql, 24] fp32 with contiguous heads")
+    from .decode import error_word
+    _lib.call("belt_prefill_attention", q.data_ptr(), ql, q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), S,
+              k.stride(0), k.stride(1), int(q_pos0), int(k_pos0), int(bool(causal)), float(scale), out.data_ptr(),
+              out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), error_word(dev).data_ptr(),
+              _stream_ptr(dev))
+    return out, lse

@@ -179,6 +179,19 @@ int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, 
                            void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, void* stream);
 
 /*
+ * Prefill attention over rebuilt keys and values: replaces the reference's flash_attn_varlen_func call in its
+ * prefill path (latent_backend.py:285-320; one request at a time). q [ql, 24, 256] BF16 (element strides q_st, q_sh,
+ * 1), k / v [num_keys, 4, 256] BF16 (kv_st, kv_sg, 1; head h reads group h / 6), query i at position q_pos0 + i, key j
+ * at k_pos0 + j; causal: key j is seen by query i when its position is not after the query's. out [ql, 24, 256] BF16
+ * (out_st, out_sh, 1) = softmax(scale q k^T) v; lse [ql, 24] fp32 (row stride lse_st, may be NULL): the natural-log
+ * sum of exp(scale q k^T) over the keys seen, -inf (and a zero output) when a query sees none.
+ */
+int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh, const void* k, const void* v,
+                           int32_t num_keys, int64_t kv_st, int64_t kv_sg, int32_t q_pos0, int32_t k_pos0,
+                           int32_t causal, float scale, void* out, int64_t out_st, int64_t out_sh, float* lse,
+                           int64_t lse_st, int32_t* err, void* stream);
+
+/*
  * Self-test of the kernels' bounded waits (no counterpart in the reference): launches one thread that waits on a
  * barrier nothing completes. The wait gives up after the same limit the decode kernel uses (~2 s), writes 0x1F0 into
  * the device word `err` (if still 0), and the kernel ends normally; status (device int32[2]) receives {2, 1} (wait gave

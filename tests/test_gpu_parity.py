@@ -581,3 +581,59 @@ def test_backend_forward_mixed_prefill():
     dec.check_device_errors(DEV)
     assert bf16_ulp_close(kv_d[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=1)
     assert_close_out(output, exp, "mixed prefill")
+
+
+# ------------------------------------------------------------------------------------------------- prefill attention
+def _attention_fp32(q, k, v, q_pos0, k_pos0, scale, causal=True):
+    """fp32 reference: q [ql, 24, D], k / v [S, 4, D]; returns (out [ql, 24, D], lse [ql, 24])."""
+    ql, S = q.shape[0], k.shape[0]
+    kh = k.float().repeat_interleave(6, dim=1)
+    vh = v.float().repeat_interleave(6, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), kh) * scale
+    if causal:
+        qp = torch.arange(ql) + q_pos0
+        kp = torch.arange(S) + k_pos0
+        s = s.masked_fill(kp[None, None, :] > qp[None, :, None], float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)                                    # [24, ql]
+    p = torch.softmax(s, dim=-1).nan_to_num(0.0)
+    return torch.einsum("hqk,khd->qhd", p, vh), lse.transpose(0, 1)
+
+
+@pytest.mark.parametrize("ql,S,q_pos0,k_pos0,causal", [
+    (1, 1, 0, 0, True), (37, 700, 663, 0, True), (300, 2050, 1750, 0, True), (129, 129, 0, 0, True),
+    (200, 500, 1000, 300, True),        # a context chunk: the queries see a prefix of the chunk's keys
+    (64, 300, 5000, 0, True),           # every key precedes every query (no mask)
+    (50, 256, 0, 100, True),            # keys after the first queries: some rows see no key (-inf, zeros)
+    (130, 777, 0, 0, False),
+])
+def test_prefill_attention(ql, S, q_pos0, k_pos0, causal):
+    g = torch.Generator().manual_seed(ql + S)
+    q = torch.randn(ql, 24, 256, generator=g).to(torch.bfloat16)
+    k = torch.randn(S, 4, 256, generator=g).to(torch.bfloat16)
+    v = torch.randn(S, 4, 256, generator=g).to(torch.bfloat16)
+    out, lse = latent_ops.prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), q_pos0, k_pos0, SCALE, causal)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    eo, el = _attention_fp32(q, k, v, q_pos0, k_pos0, SCALE, causal)
+    err = (out.float().cpu() - eo).abs()
+    assert torch.isfinite(out.float()).all()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (float(err.max()), float(err.mean()))
+    lc = lse.cpu()
+    assert torch.equal(torch.isinf(lc), torch.isinf(el))
+    live = torch.isfinite(el)
+    assert torch.allclose(lc[live], el[live], atol=1e-3, rtol=0)
+
+
+def test_prefill_attention_strided_output():
+    """Output and queries as views of the backend's [T, 24, 256] buffers (rows after the decode tokens)."""
+    g = torch.Generator().manual_seed(5)
+    qall = torch.randn(400, 24, 256, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(900, 4, 256, generator=g).to(torch.bfloat16)
+    v = torch.randn(900, 4, 256, generator=g).to(torch.bfloat16)
+    outall = torch.zeros(400, 24, 256, dtype=torch.bfloat16, device=DEV)
+    latent_ops.prefill_attention(qall[100:350], k.to(DEV), v.to(DEV), 650, 0, SCALE, out=outall[100:350])
+    torch.cuda.synchronize()
+    eo, _ = _attention_fp32(qall[100:350].cpu(), k, v, 650, 0, SCALE)
+    err = (outall[100:350].float().cpu() - eo).abs()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS
+    assert not outall[:100].any() and not outall[350:].any()
