@@ -12,9 +12,9 @@ more, joined before the decode reads the cache), then:
 * decode (one query token per request, at the front of the batch): the block-diagonal query, the split-KV decode
   kernel over the paged rows on the step's schedule (computed once per step by the builder and shared by all layers),
   the merge of each request's segments and the per-head V up-projection written straight into ``output``;
-* prefill (everything else): rows gathered through the block table, keys and values rebuilt with
-  ``LatentLayer.decompress`` and causal attention with ``torch.nn.functional.scaled_dot_product_attention``, chunked
-  with a log-sum-exp merge beyond ``PREFILL_CHUNK`` context tokens. Prefill is not the accelerated path.
+* prefill (everything else): keys and values rebuilt from the rows gathered through the block table in one tcgen05
+  kernel (``LatentLayer.decompress_paged``), causal attention on the tensor cores (``latent_ops.prefill_attention``),
+  chunked with a log-sum-exp merge beyond ``PREFILL_CHUNK`` context tokens.
 
 The classes do not depend on vLLM: ``register_with_vllm`` installs them into a vLLM that provides the plugin API.
 """
@@ -26,7 +26,6 @@ import os
 from typing import ClassVar
 
 import torch
-import torch.nn.functional as F
 
 from . import decode as dec
 from . import latent_ops
@@ -256,36 +255,35 @@ class LatentAttentionImpl:
 
     def _prefill(self, lat: LatentLayer, query: torch.Tensor, output: torch.Tensor, cache: torch.Tensor,
                  m: LatentAttentionMetadata) -> None:
-        """Each prefill request's new tokens over its whole context (causal), keys and values rebuilt from the cache rows
-        (``LatentLayer.decompress_paged``) in chunks of ``PREFILL_CHUNK`` context tokens merged by log-sum-exp."""
-        nd, page = m.num_decodes, cache.shape[1]
-        hpg = self.num_heads // lat.num_kv_heads
+        """Each prefill request's new tokens over its whole context, causal (latent_backend.py:285-320): keys and values
+        rebuilt from the cache rows on the tensor cores (``LatentLayer.decompress_paged``) in chunks of
+        ``PREFILL_CHUNK`` context tokens, the tcgen05 attention kernel over each chunk (``latent_ops.
+        prefill_attention``), chunks folded by log-sum-exp (the reference's ``merge_attn_states``)."""
+        nd = m.num_decodes
         tok = m.num_decode_tokens
         for i in range(m.num_prefills):
             b = nd + i
             ql, L = m.prefill_q_len[i], m.prefill_seq_len[i]
-            q = query[tok:tok + ql].transpose(0, 1)                      # [H, ql, D]
-            q_pos = torch.arange(L - ql, L, device=query.device)
-            out = torch.zeros(self.num_heads, ql, lat.head_dim, dtype=torch.float32, device=query.device)
-            lse = torch.full((self.num_heads, ql), float("-inf"), device=query.device)
+            q, dst = query[tok:tok + ql], output[tok:tok + ql]
             step = PREFILL_CHUNK if PREFILL_CHUNK > 0 else L
-            for c0 in range(0, L, step):
-                c1 = min(L, c0 + step)
-                pos = torch.arange(c0, c1, device=query.device)
-                # keys and values of the chunk rebuilt from the paged rows on the tensor cores
-                k, v = lat.decompress_paged(cache, m.block_table[b], L, c0, c1 - c0)
-                k = k.transpose(0, 1).repeat_interleave(hpg, dim=0).float()   # [H, S, D]
-                v = v.transpose(0, 1).repeat_interleave(hpg, dim=0).float()
-                s = torch.einsum("hqd,hsd->hqs", q.float(), k) * self.scale
-                s = s.masked_fill(pos[None, None, :] > q_pos[None, :, None], float("-inf"))
-                c_lse = torch.logsumexp(s, dim=-1)
-                c_out = torch.einsum("hqs,hsd->hqd", torch.softmax(s, dim=-1).nan_to_num(0.0), v)
-                new = torch.logaddexp(lse, c_lse)
-                w_old = torch.exp(lse - new).nan_to_num(0.0)
-                w_new = torch.exp(c_lse - new).nan_to_num(0.0)
-                out = out * w_old[..., None] + c_out * w_new[..., None]
-                lse = new
-            output[tok:tok + ql] = out.transpose(0, 1).to(output.dtype)
+            if L <= step:
+                k, v = lat.decompress_paged(cache, m.block_table[b], L, 0, L)
+                latent_ops.prefill_attention(q, k, v, L - ql, 0, self.scale, causal=True, out=dst)
+            else:
+                acc, lse = None, None
+                for c0 in range(0, L, step):
+                    c1 = min(L, c0 + step)
+                    k, v = lat.decompress_paged(cache, m.block_table[b], L, c0, c1 - c0)
+                    o_c, l_c = latent_ops.prefill_attention(q, k, v, L - ql, c0, self.scale, causal=True)
+                    if acc is None:
+                        acc, lse = o_c.float(), l_c
+                        continue
+                    new = torch.logaddexp(lse, l_c)
+                    w_old = torch.exp(lse - new).nan_to_num(0.0)
+                    w_new = torch.exp(l_c - new).nan_to_num(0.0)
+                    acc = acc * w_old[..., None] + o_c.float() * w_new[..., None]
+                    lse = new
+                dst.copy_(acc.to(dst.dtype))
             tok += ql
 
 

@@ -637,3 +637,34 @@ def test_prefill_attention_strided_output():
     err = (outall[100:350].float().cpu() - eo).abs()
     assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS
     assert not outall[:100].any() and not outall[350:].any()
+
+
+def test_backend_prefill_chunked_merge(monkeypatch):
+    """A prefill whose context spans several PREFILL_CHUNK chunks: the per-chunk attentions folded by log-sum-exp give
+    the whole-context result (the fp32 oracle)."""
+    import belt_b200.latent_backend as lb
+    monkeypatch.setattr(lb, "PREFILL_CHUNK", 384)
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=1100)
+    L, ql, page = 1000, 70, 16
+    bt, nb, _ = synth.block_tables([L], page, extra_blocks=1)
+    W = w.layout["row_width"]
+    kv = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv[:, 0], w.layout, bt, [L], seed=6, poison=False)
+    g = torch.Generator().manual_seed(15)
+    q = torch.randn(ql, 24, 256, generator=g).to(torch.bfloat16)
+    rows, rpos = oracle.gather_rows(kv[:, 0], bt, 0, L)
+    k, v = oracle.decompress(ref, rows, rpos)
+    exp, _ = _attention_fp32(q, k, v, L - ql, 0, SCALE)
+    m = lb.LatentAttentionMetadata(num_actual_tokens=ql, num_decodes=0, num_decode_tokens=0, num_prefills=1,
+                                   num_prefill_tokens=ql, block_table=bt.to(DEV),
+                                   seq_lens=torch.tensor([L], dtype=torch.int32, device=DEV), sched=None)
+    m.prefill_q_len, m.prefill_seq_len = [ql], [L]
+    impl = LatentAttentionImpl(24, 256, SCALE, 4)
+    out = torch.zeros(ql, 24, 256, dtype=torch.bfloat16, device=DEV)
+    impl._prefill(lat, q.to(DEV), out, kv.to(DEV)[:, 0], m)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    err = (out.float().cpu() - exp).abs()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (float(err.max()), float(err.mean()))
