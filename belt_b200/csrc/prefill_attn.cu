@@ -23,6 +23,13 @@
 namespace belt {
 
 namespace {
+// 2^x with the SFU's approximation (ex2.approx, flush to zero; 2^-inf = 0): P is rounded to BF16 afterwards
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 constexpr int kPaThreads = 192;
 constexpr int kPaTile = 128;
 constexpr int kPaChunk = 128 * 128;             // 128 rows x 64 channels (BF16), one swizzled chunk
@@ -164,27 +171,39 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       if (!(ok = ewait(aSFull, j & 1))) break;
       tc_fence_after();
       float s[128];
+      {
+        uint32_t r[4][32];   // the four loads in flight together, one wait
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kTmS + 32 * c, r);
+        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + kTmS + 32 * c, r[c]);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s[32 * c + e] = __uint_as_float(r[e]);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[32 * c + e] = __uint_as_float(r[c][e]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[aSFree]);
-      // scale into the exp2 domain and mask
+      // keys of this tile the row sees: all (no mask work), none, or a prefix (causal diagonal, the last tile)
       const int k0 = j * kPaTile;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 128; ++e) {
-        const int kj = k0 + e;
-        const bool valid = live_row && kj < p.S && (!p.causal || static_cast<long long>(p.k_pos0) + kj <= qpos);
-        s[e] = valid ? s[e] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[e]);
+      long long kv = p.S - k0;
+      if (p.causal) {
+        const long long lim = qpos - p.k_pos0 - k0 + 1;
+        kv = lim < kv ? lim : kv;
       }
+      const int nvis = !live_row ? 0 : kv <= 0 ? 0 : kv >= kPaTile ? kPaTile : static_cast<int>(kv);
+      float mx = -INFINITY;
+      if (nvis == kPaTile) {
+#pragma unroll
+        for (int e = 0; e < 128; ++e) mx = fmaxf(mx, s[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 128; ++e) {
+          s[e] = e < nvis ? s[e] : -INFINITY;
+          mx = fmaxf(mx, s[e]);
+        }
+      }
+      mx *= p.scale_log2;   // the row's tile max in the exp2 domain (-inf when it sees no key)
       // the previous tile's P.V has read P and written O: P can be overwritten, O rescaled
       if (j > 0 && !(ok = ewait(aPvDone, (j - 1) & 1))) break;
       tc_fence_after();
@@ -192,7 +211,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       // rescale (TMEM loads and stores, warp-collective) runs when any row of the warp needs it, alpha 1 elsewhere
       float alpha = 1.f;
       if (mx > m_run + 8.f) {
-        alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - mx);
+        alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mx);
         m_run = mx;
         l_run *= alpha;
       }
@@ -208,12 +227,15 @@ __global__ void __launch_bounds__(kPaThreads, 1)
         }
         tmem_st_wait();
       }
+      // P = exp2(scale s - m): one FFMA and one EX2 per key (masked keys hold -inf and give 0; a row that has seen no
+      // key yet uses m = 0, its scores are all -inf)
+      const float mu = m_run == -INFINITY ? 0.f : m_run;
       uint32_t pk0[32], pk1[32];
       float sum = 0.f;
 #pragma unroll
       for (int e = 0; e < 64; ++e) {
-        const float a = m_run == -INFINITY ? 0.f : exp2f(s[2 * e] - m_run);
-        const float b = m_run == -INFINITY ? 0.f : exp2f(s[2 * e + 1] - m_run);
+        const float a = fast_exp2(fmaf(s[2 * e], p.scale_log2, -mu));
+        const float b = fast_exp2(fmaf(s[2 * e + 1], p.scale_log2, -mu));
         sum += a + b;
         if (e < 32) pk0[e] = pack_bf16(a, b);
         else pk1[e - 32] = pack_bf16(a, b);
