@@ -54,6 +54,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of one baseline sample")
+    ap.add_argument("--prefill", action="store_true",
+                    help="measure the prefill path instead (one GPU): keys / values rebuilt from the paged rows and "
+                         "causal attention of 8192 new tokens over an 8192-token context, one c50 layer")
     return ap.parse_args()
 
 
@@ -397,12 +400,93 @@ def read_traffic():
         return None
 
 
+def run_prefill(args):
+    """One c50 layer's prefill of an 8192-token request through the backend's kernels: decompress of the context
+    (keys and values from the paged rows) and the causal attention, timed on the device (inputs resident, L2 flushed
+    between steps); torch's scaled_dot_product_attention on the same keys and values timed beside it."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from belt_b200 import build as _build
+    from belt_b200 import latent_ops
+    from belt_b200.layer import derive_latent_tensors
+    _build.build()
+    L, page = 8192, 16
+    w = synth.make_layer(synth.c50(), seed=synth.SEED_FACTORS)
+    lat = derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, synth.cos_sin_table(L + 1), device=dev)
+    bt, nb, _ = synth.block_tables([L], page, extra_blocks=1, seed=synth.SEED_CACHE)
+    W = w.layout["row_width"]
+    cache = torch.empty(nb, page, W, dtype=torch.bfloat16, device=dev)
+    synth.fill_cache(cache, w.layout, bt.to(dev), [L], seed=synth.SEED_CACHE, poison=False)
+    btd = bt.to(dev)
+    q = synth.make_queries(L).to(dev)
+    k = torch.empty(L, 4, 256, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(k)
+    out = torch.empty(L, 24, 256, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(L, 24, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        lat.decompress_paged(cache, btd[0], L, 0, L, k, v)
+        latent_ops.prefill_attention(q, k, v, 0, 0, SCALE, True, out, lse)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    dec.check_device_errors(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for s, e in ev:
+        flush.add_(1)
+        s.record()
+        step()
+        e.record()
+    torch.cuda.synchronize()
+    ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    qh = q.transpose(0, 1).unsqueeze(0)
+    kh = k.transpose(0, 1).repeat_interleave(6, 0).unsqueeze(0)
+    vh = v.transpose(0, 1).repeat_interleave(6, 0).unsqueeze(0)
+    lib_ms = None
+    try:
+        for _ in range(2):
+            torch.nn.functional.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=SCALE)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(3):
+            torch.nn.functional.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=SCALE)
+        e.record()
+        torch.cuda.synchronize()
+        lib_ms = s.elapsed_time(e) / 3
+    except RuntimeError:
+        pass
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak_tf = peaks.get("bf16_tflops") or 1590.0
+    flops = 24 * (L * (L + 1) / 2) * 256 * 2 * 2 + L * 2 * 256 * 4 * (320 + 512)   # attention + decompress
+    line = {"metric": "prefill tokens/s (decompress + causal attention, one c50 layer)", "value": L / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "prefill: 8192 new tokens over an 8192-token context, c50 layer, page 16",
+                       "l2": "flushed (256 MB write) before every step"},
+            "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12, "peak": peak_tf,
+                         "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / peak_tf,
+                         "peak_source": "measured" if "bf16_tflops" in peaks else "fallback"},
+            "library_sdpa_attention_ms": lib_ms, "gpu_launches": 2 * args.steps}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.prefill:
+        if rank == 0:
+            run_prefill(args)
         return
     group = dp.HostGroup()
     local = group.local_rank
