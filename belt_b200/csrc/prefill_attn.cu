@@ -4,13 +4,14 @@
 // their group's keys (24 query heads, 4 groups, head dim 256), causal by position, with the natural-log LSE of every
 // (query, head) so that the backend can fold context chunks together.
 //
-// One CTA per (128-query tile, head), 192 threads:
-//   * warp 0, lane 0: TMA producer. The query tile (128 x 256, K-major, 4 chunks of 64 columns, 128-byte swizzle)
-//     once; per 128-key tile the keys (same layout) and the values (read as the MN-major B operand: 128 key rows of
-//     64 channels per block, four blocks), each into its own single buffer;
+// One CTA per (128-query tile, head), 224 threads:
+//   * warp 0, lane 0: TMA producer of the query tile (128 x 256, K-major, 4 chunks of 64 columns, 128-byte swizzle)
+//     once and of the key tiles (same layout), warp 6, lane 0: producer of the value tiles (read as the MN-major B
+//     operand: 128 key rows of 64 channels per chunk). Each buffer holds one tile; the key buffer is refilled chunk
+//     by chunk as the score MMAs release its chunks, the value buffer as a whole once P.V has read it;
 //   * warp 1, lane 0: tcgen05 issuer. S = Q K^T (M = 128 queries, N = 128 keys, 16 steps of K = 16) into TMEM,
-//     then O += P V with P read from TMEM (M = 128, N = 256, 8 steps), software-pipelined: S of tile j + 1 is computed
-//     while the softmax turns S of tile j into P;
+//     then O += P V with P read from TMEM (M = 128, N = 256, 8 steps), software-pipelined: S of tile j + 1 is
+//     computed while the softmax turns S of tile j into P;
 //   * warps 2-5: softmax, one query row per thread (its TMEM lane): scale, mask (keys past the end or, causally,
 //     after the query's position), running max in the exp2 domain (O rescaled in TMEM only when a row's max grows by
 //     more than 2^8), P = exp2(s - m) packed to BF16 into TMEM, row sums in fp32; at the end O / l to BF16 and the
@@ -30,16 +31,16 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-constexpr int kPaThreads = 192;
+constexpr int kPaThreads = 224;
 constexpr int kPaTile = 128;
 constexpr int kPaChunk = 128 * 128;             // 128 rows x 64 channels (BF16), one swizzled chunk
 constexpr int kPaTileBytes = 4 * kPaChunk;      // 128 x 256 = 64 KB
 constexpr int kPaQ = 0, kPaK = kPaTileBytes, kPaV = 2 * kPaTileBytes;
 constexpr int kPaSmem = 3 * kPaTileBytes;       // + barriers
 constexpr uint32_t kTmS = 0, kTmP = 128, kTmO = 256;
-// barriers
-constexpr int aQ = 0, aKFull = 1, aKEmpty = 2, aVFull = 3, aVEmpty = 4, aSFull = 5, aSFree = 6, aPFull = 7,
-              aPvDone = 8, aDrain = 9, kPaBars = 10;
+// barriers: the key and value buffers are released and refilled per 64-channel chunk
+constexpr int aQ = 0, aKFull = 1, aKEmpty = 5, aVFull = 9, aVEmpty = 13, aSFull = 17, aSFree = 18, aPFull = 19,
+              aPvDone = 20, aDrain = 21, kPaBars = 22;
 }  // namespace
 
 __global__ void __launch_bounds__(kPaThreads, 1)
@@ -75,40 +76,46 @@ __global__ void __launch_bounds__(kPaThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // one chunk ring per buffer (keys: warp 0, values: warp 6): chunk c of tile j waits until the MMAs of tile j - 1
+  // that read chunk c completed, so the next tile streams in while the current one is still being multiplied
+  // nchunk = 4: one barrier pair per 64-channel chunk; nchunk = 1: the whole tile under the first pair
+  auto stream_chunks = [&](const CUtensorMap* map, int off, int full0, int empty0, int nchunk, int err_code) {
+    int issued[4] = {0, 0, 0, 0};
+    bool ok = true;
+    const int per = 4 / nchunk;
+    for (int j = 0; ok && j < n_tiles; ++j)
+#pragma unroll 1
+      for (int c = 0; c < nchunk; ++c) {
+        if (j > 0 && !(ok = mbar_wait(&bars[empty0 + c], (j - 1) & 1, abort_flag, p.err, err_code))) break;
+        mbar_arrive_expect_tx(&bars[full0 + c], per * kPaChunk);
+        for (int q = 0; q < per; ++q)
+          tma_load_3d(smem + off + (c * per + q) * kPaChunk, map, &bars[full0 + c], 64 * (c * per + q), g,
+                      j * kPaTile);
+        ++issued[c];
+      }
+    if (*abort_flag)   // the latest copy into every chunk lands before the CTA's shared memory goes away
+      for (int c = 0; c < nchunk; ++c)
+        if (issued[c]) mbar_wait_bounded(&bars[full0 + c], (issued[c] - 1) & 1, nullptr, 0, kWaitCycles / 8);
+  };
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- key producer (and the query tile)
     if (lane == 0 && n_tiles > 0) {
-      int k_issued = 0, v_issued = 0;
       mbar_arrive_expect_tx(&bars[aQ], kPaTileBytes);
 #pragma unroll
       for (int c = 0; c < 4; ++c) tma_load_3d(smem + kPaQ + c * kPaChunk, &maps.q, &bars[aQ], 64 * c, h, i0);
-      for (int j = 0; j < n_tiles; ++j) {
-        if (j > 0 && !mbar_wait(&bars[aKEmpty], (j - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&bars[aKFull], kPaTileBytes);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tma_load_3d(smem + kPaK + c * kPaChunk, &maps.k, &bars[aKFull], 64 * c, g, j * kPaTile);
-        ++k_issued;
-        if (j > 0 && !mbar_wait(&bars[aVEmpty], (j - 1) & 1, abort_flag, p.err, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(&bars[aVFull], kPaTileBytes);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tma_load_3d(smem + kPaV + c * kPaChunk, &maps.v, &bars[aVFull], 64 * c, g, j * kPaTile);
-        ++v_issued;
-      }
-      if (*abort_flag) {
-        // the latest copy into every buffer lands before the CTA's shared memory goes away
-        mbar_wait_bounded(&bars[aQ], 0, nullptr, 0, kWaitCycles / 8);
-        if (k_issued) mbar_wait_bounded(&bars[aKFull], (k_issued - 1) & 1, nullptr, 0, kWaitCycles / 8);
-        if (v_issued) mbar_wait_bounded(&bars[aVFull], (v_issued - 1) & 1, nullptr, 0, kWaitCycles / 8);
-      }
+      stream_chunks(&maps.k, kPaK, aKFull, aKEmpty, 4, kErrTimeoutProducer);
+      if (*abort_flag) mbar_wait_bounded(&bars[aQ], 0, nullptr, 0, kWaitCycles / 8);
     }
+    __syncwarp();
+  } else if (warp == 6) {
+    // ---------------------------------------------------------------- value producer
+    if (lane == 0 && n_tiles > 0) stream_chunks(&maps.v, kPaV, aVFull, aVEmpty, 1, kErrTimeoutProducer);
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- tcgen05 issuer
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128, 0, 0);   // Q K-major, K K-major
-      constexpr uint32_t idO = idesc_bf16(128, 256, 0, 1);   // P from TMEM, V MN-major
+      constexpr uint32_t idO = idesc_bf16(128, 256, 0, 1);   // P from TMEM, V MN-major (four 64-channel blocks)
       constexpr uint32_t hiSw = desc_hi(1024, kSwizzle128);
       const uint32_t base = smem_u32(smem);
       bool ok = true;
@@ -116,22 +123,25 @@ __global__ void __launch_bounds__(kPaThreads, 1)
         return mbar_wait(&bars[bar], parity, abort_flag, p.err, kErrTimeoutMma);
       };
       auto qk = [&](int j) -> bool {
-        if (!wait(aKFull, j & 1)) return false;
         if (j > 0 && !wait(aSFree, (j - 1) & 1)) return false;   // the softmax has read S of the previous tile
-        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          if (!wait(aKFull + c, j & 1)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int s = 0; s < 16; ++s) {
-          const uint32_t off = (s >> 2) * kPaChunk + (s & 3) * 32;
-          mma_ss(tmem + kTmS, desc_of(desc_lo(base + kPaQ + off, 16), hiSw),
-                 desc_of(desc_lo(base + kPaK + off, 16), hiSw), idS, s ? 1u : 0u);
+          for (int s = 0; s < 4; ++s) {
+            const uint32_t off = c * kPaChunk + s * 32;
+            mma_ss(tmem + kTmS, desc_of(desc_lo(base + kPaQ + off, 16), hiSw),
+                   desc_of(desc_lo(base + kPaK + off, 16), hiSw), idS, (c | s) ? 1u : 0u);
+          }
+          mma_commit(&bars[aKEmpty + c]);   // key chunk c of this tile read
         }
-        mma_commit(&bars[aKEmpty]);
         mma_commit(&bars[aSFull]);
         return true;
       };
       auto pv = [&](int j) -> bool {
-        if (!wait(aVFull, j & 1)) return false;
         if (!wait(aPFull, j & 1)) return false;
+        if (!wait(aVFull, j & 1)) return false;
         tc_fence_after();
 #pragma unroll
         for (int s = 0; s < 8; ++s)
@@ -153,7 +163,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 6) {
     // ---------------------------------------------------------------- softmax warps (rows of TMEM lane quadrant)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
