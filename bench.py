@@ -338,7 +338,8 @@ def run_reference_arm(args, rank, world):
 def e2e_rate(wl: Workload, steps: int, warmup: int):
     """Decode tokens/s through the backend's public surface (``latent_attention_step``: the fused down-projection
     cache write, then ``LatentAttentionImpl.forward``), with this step's inputs (queries, layer inputs of the new
-    tokens, positions) copied from pinned host memory and the attention outputs copied back inside the timed region."""
+    tokens, positions) copied from pinned host memory and the attention outputs copied back inside the timed region,
+    on a copy stream that overlaps them with the layers' compute."""
     from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl,
                                           LatentAttentionMetadataBuilder, LatentKVSpec, latent_attention_step)
     dev = wl.device
@@ -363,17 +364,34 @@ def e2e_rate(wl: Workload, steps: int, warmup: int):
     qsl = torch.arange(B + 1, dtype=torch.int32)
     qsl_dev = qsl.to(dev)
 
+    # the copies run on their own stream: every layer's inputs go up at the start of the step, layer l waits only for
+    # its own, and its output goes down as soon as it is written, while the next layers compute; the step ends when
+    # the last output has landed in host memory
+    copy = torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(L)]
+    out_done = [torch.cuda.Event() for _ in range(L)]
+
     def one():
-        q_dev.copy_(q_host, non_blocking=True)
-        x_dev.copy_(x_host, non_blocking=True)
-        pos_dev.copy_(pos_host, non_blocking=True)
+        main = torch.cuda.current_stream(dev)
+        copy.wait_stream(main)
+        with torch.cuda.stream(copy):
+            pos_dev.copy_(pos_host, non_blocking=True)
+            for l in range(L):
+                q_dev[l].copy_(q_host[l], non_blocking=True)
+                x_dev[l].copy_(x_host[l], non_blocking=True)
+                in_ready[l].record(copy)
         cm = CommonAttentionMetadata(query_start_loc=qsl_dev, query_start_loc_cpu=qsl, seq_lens=wl.seq_lens,
                                      block_table_tensor=wl.block_table, slot_mapping=wl.slots, num_reqs=B,
                                      num_actual_tokens=B, max_query_len=1)
         md = builder.build(0, cm)
         for l in range(L):
+            main.wait_event(in_ready[l])
             latent_attention_step(impl, layer_objs[l], q_dev[l], x_dev[l], wl.w_down[l], kv[:, l], md, out_dev[l])
-        out_host.copy_(out_dev, non_blocking=True)
+            out_done[l].record(main)
+            copy.wait_event(out_done[l])
+            with torch.cuda.stream(copy):
+                out_host[l].copy_(out_dev[l], non_blocking=True)
+        main.wait_stream(copy)
 
     for _ in range(warmup):
         one()
