@@ -35,6 +35,9 @@ SIGNATURES = {
                                c_i32p, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
     "belt_prefill_attention": [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_f32,
                                c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
+    "belt_q_norm_rope": [c_vp, c_i32, c_i64, c_i64, c_vp, c_f32, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_i64, c_i64,
+                         c_vp],
+    "belt_gate_mul": [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i32, c_vp, c_i64, c_i64, c_vp],
     "belt_selftest_bounded_wait": [c_vp, c_vp, c_vp],
     "belt_num_sms": [c_i32],
     "belt_abi_version": [],

@@ -703,6 +703,40 @@ int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh
   return e == cudaSuccess ? ok() : cuda_fail(e, "prefill_attention launch");
 }
 
+int belt_q_norm_rope(const void* qg, int32_t num_tokens, int64_t qg_st, int64_t qg_sh, const float* norm_weight,
+                     float eps, const void* cos_sin, int32_t max_pos, int32_t rot, const void* positions,
+                     int32_t positions_i64, void* q, int64_t q_st, int64_t q_sh, void* stream) {
+  using namespace belt;
+  if (num_tokens < 0 || rot < 16 || rot > 256 || rot % 16 || max_pos < 1 || eps < 0.f)
+    return fail(BELT_ERR_INVALID, "q_norm_rope: tokens %d, rot %d (a multiple of 16 up to 256), max_pos %d", num_tokens,
+                rot, max_pos);
+  if (num_tokens == 0) return ok();
+  if (!qg || !norm_weight || !cos_sin || !positions || !q) return fail(BELT_ERR_INVALID, "q_norm_rope: null buffer");
+  if (!aligned16(qg) || !aligned16(q) || qg_st % 8 || qg_sh % 8 || q_st % 8 || q_sh % 8 || q_sh < 256 ||
+      q_st < kH * q_sh)
+    return fail(BELT_ERR_INVALID, "q_norm_rope: 16-byte aligned rows, strides multiples of 8 elements");
+  QNormRopeParams p{static_cast<const __nv_bfloat16*>(qg), qg_st, qg_sh, num_tokens, kH, norm_weight, eps,
+                    static_cast<const __nv_bfloat16*>(cos_sin), max_pos, rot, positions, positions_i64 ? 1 : 0,
+                    static_cast<__nv_bfloat16*>(q), q_st, q_sh};
+  cudaError_t e = launch_q_norm_rope(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "q_norm_rope launch");
+}
+
+int belt_gate_mul(const void* attn, int64_t attn_st, int64_t attn_sh, const void* gate, int64_t gate_st,
+                  int64_t gate_sh, int32_t num_tokens, void* out, int64_t out_st, int64_t out_sh, void* stream) {
+  using namespace belt;
+  if (num_tokens < 0) return fail(BELT_ERR_INVALID, "gate_mul: tokens %d", num_tokens);
+  if (num_tokens == 0) return ok();
+  if (!attn || !gate || !out) return fail(BELT_ERR_INVALID, "gate_mul: null buffer");
+  if (!aligned16(attn) || !aligned16(gate) || !aligned16(out) || attn_st % 8 || attn_sh % 8 || gate_st % 8 ||
+      gate_sh % 8 || out_st % 8 || out_sh % 8)
+    return fail(BELT_ERR_INVALID, "gate_mul: 16-byte aligned rows, strides multiples of 8 elements");
+  GateMulParams p{static_cast<const __nv_bfloat16*>(attn), attn_st, attn_sh, static_cast<const __nv_bfloat16*>(gate),
+                  gate_st, gate_sh, num_tokens, kH, static_cast<__nv_bfloat16*>(out), out_st, out_sh};
+  cudaError_t e = launch_gate_mul(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "gate_mul launch");
+}
+
 int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream) {
   if (!err || !status) return fail(BELT_ERR_INVALID, "selftest_bounded_wait: null buffer");
   cudaError_t e = belt::launch_selftest_wait(err, status, as_stream(stream));

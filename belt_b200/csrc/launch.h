@@ -202,6 +202,32 @@ struct PrefillAttnParams {
 };
 cudaError_t launch_prefill_attn(const PrefillAttnMaps& maps, const PrefillAttnParams& p, cudaStream_t stream);
 
+// Element-wise steps around the attention (model_ops.cu).
+struct QNormRopeParams {
+  const __nv_bfloat16* qg;   // [T, H, >= 256] (the query half of each head's q_gate_proj block)
+  long long qg_st, qg_sh;
+  int T, H;
+  const float* w;            // [256] zero-centred RMSNorm weight
+  float eps;
+  const __nv_bfloat16* cos_sin;   // [max_pos, rot]
+  int max_pos, rot;
+  const void* positions;
+  int pos_i64;
+  __nv_bfloat16* q;
+  long long q_st, q_sh;
+};
+cudaError_t launch_q_norm_rope(const QNormRopeParams& p, cudaStream_t stream);
+struct GateMulParams {
+  const __nv_bfloat16* attn;
+  long long attn_st, attn_sh;
+  const __nv_bfloat16* gate;
+  long long gate_st, gate_sh;
+  int T, H;
+  __nv_bfloat16* out;
+  long long out_st, out_sh;
+};
+cudaError_t launch_gate_mul(const GateMulParams& p, cudaStream_t stream);
+
 // Bounded-wait self-test (selftest.cu).
 cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);
 

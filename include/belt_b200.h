@@ -192,6 +192,24 @@ int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh
                            int64_t lse_st, int32_t* err, void* stream);
 
 /*
+ * The query side of the model's fused q-norm / RoPE (models/qwen3_5_latent.py:209-212, `fused_qk_rmsnorm_rope_gate`
+ * with no key heads): qg [T, 24, >= 256] BF16 (element strides qg_st, qg_sh, 1; the query half of every head's
+ * q_gate_proj block) -> q [T, 24, 256] BF16 = NeoX rotation of the first `rot` channels (BF16 cos / sin table
+ * [max_pos, rot], cos then sin) of x * rsqrt(mean(x^2) + eps) * (1 + norm_weight) (fp32, zero-centred RMSNorm weight
+ * [256] fp32), rounded to BF16 once. positions [T] int32 or int64 (positions_i64).
+ */
+int belt_q_norm_rope(const void* qg, int32_t num_tokens, int64_t qg_st, int64_t qg_sh, const float* norm_weight,
+                     float eps, const void* cos_sin, int32_t max_pos, int32_t rot, const void* positions,
+                     int32_t positions_i64, void* q, int64_t q_st, int64_t q_sh, void* stream);
+
+/*
+ * The output gate (models/qwen3_5_latent.py:215): out = attn * sigmoid(gate), all [T, 24, 256] BF16 views with
+ * element strides (st, sh, 1); out may alias attn.
+ */
+int belt_gate_mul(const void* attn, int64_t attn_st, int64_t attn_sh, const void* gate, int64_t gate_st,
+                  int64_t gate_sh, int32_t num_tokens, void* out, int64_t out_st, int64_t out_sh, void* stream);
+
+/*
  * Self-test of the kernels' bounded waits (no counterpart in the reference): launches one thread that waits on a
  * barrier nothing completes. The wait gives up after the same limit the decode kernel uses (~2 s), writes 0x1F0 into
  * the device word `err` (if still 0), and the kernel ends normally; status (device int32[2]) receives {2, 1} (wait gave

@@ -30,7 +30,7 @@ __all__ = [
     "H", "G", "D", "ROT", "CHUNK", "HPG", "ALIGN", "align", "k_segments", "row_layout", "rope_basis",
     "build_latent_layer", "rope_cos_sin", "derive", "rope_blocks", "latent_rows", "project_rows", "block_diag_query",
     "block_diag_query_construct", "up_project", "decompress", "attend", "gather_rows", "decode_reference",
-    "decode_fp32", "schedule", "schedule_weighted", "decode_partials", "merge_segments", "decode_kernel_path",
+    "decode_fp32", "q_norm_rope", "gate_mul", "schedule", "schedule_weighted", "decode_partials", "merge_segments", "decode_kernel_path",
 ]
 
 
@@ -310,6 +310,25 @@ def decode_fp32(q, cache, block_table, seq_lens, layer, scale):
         v = torch.einsum("sr,grd->sgd", rows[:, vo:vo + vr], Uv)
         out[b] = attend(q[b].float(), k, v, scale)
     return out
+
+
+def q_norm_rope(qg, norm_weight, eps, cos_sin, positions):
+    """The query side of the model's fused q-norm / RoPE (``models/qwen3_5_latent.py:209-212``): qg [T, H, >= D] ->
+    [T, H, D] BF16 = NeoX rotation of the first rot channels (cos_sin [max_pos, rot] BF16, cos then sin) of
+    x * rsqrt(mean(x^2) + eps) * (1 + w) (the Qwen3.5 zero-centred RMSNorm), fp32 throughout, one BF16 rounding."""
+    D_ = norm_weight.shape[0]
+    x = qg[..., :D_].float()
+    x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + norm_weight.float())
+    rot = cos_sin.shape[1]
+    cs = cos_sin[positions.long()].float()                    # [T, rot]
+    cos, sin = cs[:, None, :rot // 2], cs[:, None, rot // 2:]
+    x1, x2 = x[..., :rot // 2], x[..., rot // 2:rot]
+    return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin, x[..., rot:]), dim=-1).to(torch.bfloat16)
+
+
+def gate_mul(attn, gate):
+    """attn * sigmoid(gate) (``models/qwen3_5_latent.py:215``), fp32, BF16 out."""
+    return (attn.float() * torch.sigmoid(gate.float())).to(torch.bfloat16)
 
 
 def schedule(seq_lens, num_ctas, tile, min_tiles=1, capacity=None):

@@ -668,3 +668,75 @@ def test_backend_prefill_chunked_merge(monkeypatch):
     dec.check_device_errors(DEV)
     err = (out.float().cpu() - exp).abs()
     assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (float(err.max()), float(err.mean()))
+
+
+# ------------------------------------------------------------------------------------------------- model-side block
+def test_q_norm_rope_and_gate_mul():
+    """The query-side norm / RoPE and the output gate against their fp32 restatements: q within 1 BF16 ulp, the gate
+    within 2 (the kernel's exp approximation)."""
+    from belt_b200 import model
+    g = torch.Generator().manual_seed(41)
+    T = 300
+    qg = (torch.randn(T, 24, 512, generator=g) * 3).to(torch.bfloat16)
+    w = torch.randn(256, generator=g) * 0.1
+    cos_sin = synth.cos_sin_table(4096).to(torch.bfloat16)   # the layer's BF16 table
+    pos = torch.randint(0, 4096, (T,), generator=g)
+    for dtype in (torch.int64, torch.int32):
+        q = model.q_norm_rope(qg.to(DEV)[:, :, :256], w, 1e-6, cos_sin.to(DEV), pos.to(dtype).to(DEV))
+        torch.cuda.synchronize()
+        assert bf16_ulp_close(q.cpu(), oracle.q_norm_rope(qg, w, 1e-6, cos_sin, pos), ulps=1, atol=1e-6)
+    attn = torch.randn(T, 24, 256, generator=g).to(torch.bfloat16)
+    out = model.gate_mul(attn.to(DEV), qg.to(DEV)[:, :, 256:])
+    torch.cuda.synchronize()
+    assert bf16_ulp_close(out.cpu(), oracle.gate_mul(attn, qg[:, :, 256:]), ulps=2, atol=1e-6)
+
+
+def test_latent_self_attention_block():
+    """The whole attention block of a compressed layer (q_gate GEMM, q-norm / RoPE, fused write, decode, gate, o_proj)
+    for one decode step, against the fp32 oracle chain."""
+    from belt_b200 import model
+    spec = synth.spec_from_ranks(512, 512)
+    w = synth.make_layer(spec)
+    hidden_size = w.kv_latent_proj.shape[1]
+    g = torch.Generator().manual_seed(42)
+    q_gate = (torch.randn(24 * 512, hidden_size, generator=g) / hidden_size ** 0.5).to(torch.bfloat16)
+    o_proj = (torch.randn(hidden_size, 24 * 256, generator=g) / (24 * 256) ** 0.5).to(torch.bfloat16)
+    q_norm = torch.randn(256, generator=g) * 0.1
+    cos_sin = synth.cos_sin_table(3000)
+    blk = model.LatentSelfAttention(q_gate, o_proj, q_norm, w.k_norm_weight, w.kv_latent_proj, w.k_up, w.v_up,
+                                    w.layout, cos_sin, device=DEV)
+    ref = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin)
+    seqs = [300, 1, 2049, 129, 700]
+    page = 16
+    bt, nb, _ = synth.block_tables(seqs, page, extra_blocks=2)
+    W = w.layout["row_width"]
+    kv = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv[:, 0], w.layout, bt, seqs, seed=7, poison=False)
+    B = len(seqs)
+    hidden = torch.randn(B, hidden_size, generator=g).to(torch.bfloat16)
+    pos = torch.tensor(seqs) - 1
+    slots = bt[torch.arange(B), pos // page].long() * page + pos % page
+    # expected: the fp32 chain with the reference's roundings
+    qg = (hidden.float() @ q_gate.float().T).to(torch.bfloat16).view(B, 24, 512)
+    q = oracle.q_norm_rope(qg, q_norm, 1e-6, cos_sin.to(torch.bfloat16), pos)
+    exp_cache = oracle.project_rows(hidden, w.kv_latent_proj, slots, kv[:, 0].clone(), ref["u_cat"], ref["k_segs"],
+                                    1e-6)
+    att = oracle.decode_fp32(q, exp_cache, bt, torch.tensor(seqs), ref, 1 / 16).to(torch.bfloat16)
+    gated = oracle.gate_mul(att, qg[:, :, 256:])
+    exp = gated.float().view(B, -1) @ o_proj.float().T
+
+    spec_kv = LatentKVSpec(block_size=page, num_kv_heads=1, head_size=W)
+    builder = LatentAttentionMetadataBuilder(spec_kv, ["l0"], device=DEV, max_num_batched_tokens=256)
+    cm = CommonAttentionMetadata(query_start_loc=torch.arange(B + 1, dtype=torch.int32, device=DEV),
+                                 query_start_loc_cpu=torch.arange(B + 1, dtype=torch.int32),
+                                 seq_lens=torch.tensor(seqs, dtype=torch.int32, device=DEV),
+                                 block_table_tensor=bt.to(DEV), slot_mapping=slots.to(DEV), num_reqs=B,
+                                 num_actual_tokens=B, max_query_len=1)
+    md = builder.build(0, cm)
+    out = blk.forward(pos.to(DEV), hidden.to(DEV), kv.to(DEV), md)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    err = (out.float().cpu() - exp).abs()
+    scale = float(exp.abs().max())
+    assert float(err.max()) < 2e-2 * max(1.0, scale) and float(err.mean()) < 2e-3 * max(1.0, scale), \
+        (float(err.max()), float(err.mean()), scale)
