@@ -214,6 +214,9 @@ class ClockSampler:
             time.sleep(0.01)
 
     def start(self):
+        # the timed loop is Python issuing launches: a 1 ms interpreter switch interval lets the sampling thread run
+        self.switch = sys.getswitchinterval()
+        sys.setswitchinterval(0.001)
         try:
             import threading
             nv, h = self._nvml_handle()
@@ -251,6 +254,7 @@ class ClockSampler:
         os.unlink(self.path)
 
     def stop(self) -> dict:
+        sys.setswitchinterval(getattr(self, "switch", 0.005))
         if self.thread is not None:
             self.stop_flag = True
             self.thread.join(timeout=5)
