@@ -73,3 +73,27 @@ def test_schedule_rejects_small_capacity(lib):
 def test_python_layer_raises_value_error(lib):
     with pytest.raises(ValueError):
         _lib.call("belt_latent_decode", *_decode_args(page=24))
+
+
+def test_new_entries_reject_bad_arguments(lib):
+    """The prefill and model-side entries refuse bad arguments before touching the device."""
+    import ctypes
+    segs = _lib.int_array([0, 128, 0, 0] * 4)
+    # decompress: positions past the request, an unsupported page size
+    assert lib.belt_latent_decompress(16, 10, 16, 1024, 16384, 1024, 16, 100, 90, 20, 16, 512, segs, 16, 512, 512,
+                                      16, 4096, 16, 16, 1024, 256, 0, 0) == -1
+    assert b"outside" in lib.belt_last_error()
+    assert lib.belt_latent_decompress(16, 10, 24, 1024, 16384, 1024, 16, 100, 0, 20, 16, 512, segs, 16, 512, 512,
+                                      16, 4096, 16, 16, 1024, 256, 0, 0) == -1
+    assert b"page size" in lib.belt_last_error()
+    # prefill attention: misaligned query, bad strides
+    assert lib.belt_prefill_attention(8, 10, 6144, 256, 16, 16, 10, 1024, 256, 0, 0, 1, ctypes.c_float(0.0625), 16,
+                                      6144, 256, None, 24, 0, 0) == -1
+    assert b"aligned" in lib.belt_last_error()
+    # q-norm / RoPE: a rotary width that is not a multiple of 16
+    assert lib.belt_q_norm_rope(16, 4, 12288, 512, 16, ctypes.c_float(1e-6), 16, 4096, 24, 16, 1, 16, 6144, 256,
+                                0) == -1
+    assert b"rot" in lib.belt_last_error()
+    # gate: misaligned output
+    assert lib.belt_gate_mul(16, 6144, 256, 16, 12288, 512, 4, 8, 6144, 256, 0) == -1
+    assert b"aligned" in lib.belt_last_error()
