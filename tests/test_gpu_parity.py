@@ -263,7 +263,7 @@ def test_up_project(name):
 def test_merge_segments():
     g = torch.Generator().manual_seed(2)
     for seqs, nct, lv in [([129, 513, 1025, 2001], 16, 512), ([0, 300, 64, 0], 8, 96), ([40] * 12, 8, 640),
-                          ([9000] * 3, 148, 512)]:
+                          ([9000] * 3, 148, 512), ([300 * 128], 300, 64)]:
         B = len(seqs)
         sched = dec.make_schedule(B, DEV, num_ctas=nct)
         dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
