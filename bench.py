@@ -48,7 +48,9 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=3, choices=[2, 3])
+    ap.add_argument("--config", type=int, default=3, choices=[2, 3, 4])
+    ap.add_argument("--rows", default="c50", choices=["c50", "c25"],
+                    help="config 4 row format: c50 (r_k = r_v = 512, 1024-column rows) or c25 (256 + 256, 512 columns)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
@@ -61,12 +63,18 @@ def parse_args():
 
 
 # ------------------------------------------------------------------------------------------------------------ workload
-def workload_spec(config: int, batch: int | None, rank: int, world: int):
+def workload_spec(config: int, batch: int | None, rank: int, world: int, rows: str = "c50"):
     """(layer specs, this rank's seq_lens, page, description, partition imbalance). The box holds batch x world
     requests; ranks take LPT shares by context tokens (equal counts), so every rank decodes ~batch requests."""
     if config == 2:
         B = batch or 64
         return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}, 1.0
+    if config == 4:
+        # long context: every request 65,536 cached tokens + this step's, 512 tiles each over the CTAs
+        B = batch or 32
+        spec = synth.c25() if rows == "c25" else synth.c50()
+        return [spec] * 16, [65536 + 1] * B, 16, {
+            "workload": f"config4: 16 layers {rows} (rows of {spec.row_width} columns), batch 32 x 65536, page 16"}, 1.0
     B = batch or 128
     ranks = synth.learned_ranks(16)
     pool = synth.log_uniform_lengths(B * world, 1024, 65536, seed=synth.SEED_LENGTHS)
@@ -318,8 +326,8 @@ def run_reference_arm(args, rank, world):
     """The reference's CPU path on the whole box's requests (every rank's share), rank 0 only."""
     if rank != 0:
         return
-    per_gpu = args.batch or (64 if args.config == 2 else 128)
-    specs, seq_lens, page, cfg, _ = workload_spec(args.config, per_gpu * world, 0, 1)
+    per_gpu = args.batch or {2: 64, 3: 128, 4: 32}[args.config]
+    specs, seq_lens, page, cfg, _ = workload_spec(args.config, per_gpu * world, 0, 1, args.rows)
     rates, tsum = [], 0.0
     for i in range(args.warmup + args.steps):
         budget = min(args.cpu_seconds, 240.0 / max(1, args.warmup + args.steps))
@@ -516,7 +524,7 @@ def main():
     dev = torch.device("cuda", local)
     from belt_b200 import build as _build
     _build.build()
-    specs, seq_lens, page, cfg, imb = workload_spec(args.config, args.batch, rank, world)
+    specs, seq_lens, page, cfg, imb = workload_spec(args.config, args.batch, rank, world, args.rows)
     wl = Workload(specs, seq_lens, page, dev, rank)
     torch.cuda.synchronize()
 

@@ -427,6 +427,88 @@ def test_backend_forward_decode_step():
     assert_close_out(out_f, exp, "fused step")
 
 
+def test_backend_decode_cuda_graph():
+    """UNIFORM_SINGLE_TOKEN_DECODE graphs: the decode forward (side-stream cache write, absorbed query, split-KV
+    decode, merge, U_v projection) captured once and replayed for two more steps whose inputs and metadata were
+    refilled in place (contexts one token longer each step, new queries and new rows; the builder recomputes the
+    schedule into its persistent buffers outside the graph). Every replay equals the eager forward of the same step,
+    bit for bit, and so do the caches."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    seqs0 = [40, 300, 1, 2050, 129] * 8
+    B, page, steps = len(seqs0), 16, 3
+    bt, nb, _ = synth.block_tables([s + steps for s in seqs0], page, extra_blocks=2)
+    W = w.layout["row_width"]
+    kv0 = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv0[:, 0], w.layout, bt, [s + steps for s in seqs0], seed=23, poison=False)
+    g = torch.Generator().manual_seed(24)
+    inputs = []
+    for k in range(steps):
+        seqs = torch.tensor([s + k for s in seqs0], dtype=torch.int32)
+        pos = seqs.long() - 1
+        slots = bt[torch.arange(B), pos // page].long() * page + pos % page
+        x = torch.randn(B, w.kv_latent_proj.shape[1], generator=g).to(torch.bfloat16)
+        c = (x.float() @ w.kv_latent_proj.float().T).to(torch.bfloat16)
+        q = torch.randn(B, 24, 256, generator=g).to(torch.bfloat16)
+        inputs.append((seqs, pos, slots, c, q))
+    spec_kv = LatentKVSpec(block_size=page, num_kv_heads=1, head_size=W)
+    builder = LatentAttentionMetadataBuilder(spec_kv, ["l0"], device=DEV, max_num_batched_tokens=256)
+    impl = LatentAttentionImpl(24, 256, SCALE, 4)
+
+    class Layer:
+        latent = lat
+    # persistent device buffers, refilled in place before every step
+    seq_d = torch.empty(B, dtype=torch.int32, device=DEV)
+    pos_d = torch.empty(B, dtype=torch.int64, device=DEV)
+    slot_d = torch.empty(B, dtype=torch.int64, device=DEV)
+    c_d = torch.empty(B, W, dtype=torch.bfloat16, device=DEV)[:, :c.shape[1]]
+    q_d = torch.empty(B, 24, 256, dtype=torch.bfloat16, device=DEV)
+    out_d = torch.empty(B, 24, 256, dtype=torch.bfloat16, device=DEV)
+    bt_d = bt.to(DEV)
+    qsl = torch.arange(B + 1, dtype=torch.int32)
+
+    def refill(k):
+        seqs, pos, slots, c, q = inputs[k]
+        seq_d.copy_(seqs)
+        pos_d.copy_(pos)
+        slot_d.copy_(slots)
+        c_d.copy_(c)
+        q_d.copy_(q)
+        cm = CommonAttentionMetadata(query_start_loc=qsl.to(DEV), query_start_loc_cpu=qsl, seq_lens=seq_d,
+                                     block_table_tensor=bt_d, slot_mapping=slot_d, num_reqs=B, num_actual_tokens=B,
+                                     max_query_len=1)
+        return builder.build(0, cm)
+
+    # eager reference: all steps in order
+    kv_e = kv0.to(DEV)
+    eager = []
+    for k in range(steps):
+        md = refill(k)
+        impl.forward(Layer, q_d, c_d, pos_d, kv_e, md, out_d)
+        eager.append(out_d.clone())
+    torch.cuda.synchronize()
+    # graph: step 0 eagerly on a side stream (warm-up), capture, then replay steps 1 and 2
+    kv_g = kv0.to(DEV)
+    md = refill(0)
+    s = torch.cuda.Stream(DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(s):
+        impl.forward(Layer, q_d, c_d, pos_d, kv_g, md, out_d)
+    torch.cuda.current_stream(DEV).wait_stream(s)
+    assert torch.equal(out_d, eager[0])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        impl.forward(Layer, q_d, c_d, pos_d, kv_g, md, out_d)
+    for k in range(1, steps):
+        refill(k)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_d, eager[k]), k
+    dec.check_device_errors(DEV)
+    assert torch.equal(kv_g, kv_e)
+
+
 def test_decode_long_context_properties():
     """Config-2 size (B = 64, L = 8192, c50): finite, matches the oracle on a sample of requests, and a request's
     output does not depend on the others in the batch."""
