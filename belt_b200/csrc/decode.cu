@@ -23,7 +23,8 @@
 // * warp 2, query loader (lanes 0-15): a segment's block-diagonal query chunks, once the previous segment released them.
 // * warp 3: idle.
 // * warps 4-7, rotation: BF16(gain * B_g c~) -> NeoX rotation at each token's position in fp32 -> BF16 operand
-//   (cute_decode.py:473-484), one TMEM lane (token) per thread.
+//   (cute_decode.py:473-484), one TMEM lane (token) per thread; in packed fp32x2 arithmetic for narrow rows
+//   (kPackedRot).
 // * warps 8-11, softmax: masked online softmax in the exp2 domain; the running max of a head is raised only when a
 //   tile exceeds it by more than 2^8 (a warp vote; the O rescale then waits for the previous P.V), P rounded to BF16
 //   (cute_decode.py:408); per segment the normalised partial output and its natural-log LSE (cute_decode.py:435-455).
