@@ -5,6 +5,8 @@
 //     row[lk : W] = c[lk : W] (V latent and alignment gaps, unscaled); slot < 0 (padding) is skipped.
 // Block (x, g): 16 tokens of group g (g < G) or the V-part copy (g == G). For a group, 256 threads = 256 channels;
 // the 16 tokens' latent coordinates sit in shared memory and every U_g row is read once per block.
+// belt_latent_rows_to_cache uses this kernel only for layouts the fused write's c-input mode (proj_write.cu) does not
+// take: a group spread over more than five 64-column chunks, or a u_cat that is not 16-byte aligned.
 #include "common.cuh"
 #include "launch.h"
 

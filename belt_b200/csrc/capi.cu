@@ -236,6 +236,51 @@ int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_s
   return r == BELT_OK ? ok() : r;
 }
 
+// Work items of the fused write (proj_write.cu) for a row layout: every group's 64-column window, then the V part
+// [lk, W) in windows of two chunks; also the groups' runs. Returns BELT_OK or fails with `who` in the message.
+static int pw_items(belt::ProjWriteParams& p, const int32_t* k_segs, int32_t lk, int32_t row_width, const char* who) {
+  int items = 0;
+  for (int g = 0; g < belt::kG; ++g) {
+    p.a_lo[g] = k_segs[4 * g];
+    p.a_n[g] = k_segs[4 * g + 1];
+    p.b_lo[g] = k_segs[4 * g + 2];
+    p.b_n[g] = k_segs[4 * g + 3];
+    const int r = p.a_n[g] + p.b_n[g];
+    if (p.a_lo[g] < 0 || p.b_lo[g] < 0 || p.a_n[g] < 0 || p.b_n[g] < 0 || r > 256 ||
+        p.a_lo[g] + p.a_n[g] > lk || (p.b_n[g] > 0 && p.b_lo[g] + p.b_n[g] > lk))
+      return fail(BELT_ERR_INVALID, "%s: k_segs of group %d out of range (lk %d)", who, g, lk);
+    bool use[64] = {};
+    const int runs[2][2] = {{p.a_lo[g], p.a_n[g]}, {p.b_lo[g], p.b_n[g]}};
+    for (int q = 0; q < 2; ++q)
+      if (runs[q][1] > 0)
+        for (int c = runs[q][0] >> 6; c <= (runs[q][0] + runs[q][1] - 1) >> 6 && c < 64; ++c) use[c] = true;
+    int n = 0;
+    for (int c = 0; c < 64; ++c)
+      if (use[c]) {
+        if (n == belt::kPwMaxChunks)
+          return fail(BELT_ERR_INVALID, "%s: group %d spans more than %d 64-column chunks", who, g,
+                      belt::kPwMaxChunks);
+        p.item_chunk[items][n++] = c;
+      }
+    if (n == 0) {   // a group without coordinates still gets an item (nothing to write); keep one chunk to stream
+      p.item_chunk[items][0] = 0;
+      n = 1;
+    }
+    p.item_nch[items++] = n;
+  }
+  // V part in windows of two 64-column chunks: more CTAs, each streaming a smaller share of W_down
+  constexpr int kVChunks = 2;
+  for (int c = lk >> 6; c < (row_width + 63) >> 6; c += kVChunks) {
+    if (items == belt::kPwMaxItems)
+      return fail(BELT_ERR_INVALID, "%s: V part too wide (%d columns)", who, row_width - lk);
+    const int n = ((row_width + 63) >> 6) - c < kVChunks ? ((row_width + 63) >> 6) - c : kVChunks;
+    for (int i = 0; i < n; ++i) p.item_chunk[items][i] = c + i;
+    p.item_nch[items++] = n;
+  }
+  p.n_items = items;
+  return BELT_OK;
+}
+
 int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, const void* slots, int32_t slots_i64,
                               void* cache, int64_t num_blocks, int32_t page, int32_t row_width, int64_t stride_block,
                               int64_t stride_tok, const void* u_cat, int32_t lk, const int32_t* k_segs, float eps,
@@ -269,6 +314,38 @@ int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, c
     if (p.a_lo[g] < 0 || p.b_lo[g] < 0 || p.a_n[g] < 0 || p.b_n[g] < 0 || r > 256 ||
         p.a_lo[g] + p.a_n[g] > lk || (p.b_n[g] > 0 && p.b_lo[g] + p.b_n[g] > lk))
       return fail(BELT_ERR_INVALID, "latent_rows_to_cache: k_segs of group %d out of range (lk %d)", g, lk);
+  }
+  // The fused write's kernel in c-input mode (RMS fold on the tensor cores) wherever the layout fits it: every group
+  // within five 64-column chunks, u_cat 16-byte aligned. Otherwise the SIMT kernel below.
+  if (lk > 0 && stride_tok >= row_width && aligned16(u_cat) && num_tokens <= (1ll << 31) - 1) {
+    belt::ProjWriteParams q{};
+    q.slots = slots;
+    q.slots_i64 = slots_i64 ? 1 : 0;
+    q.num_slots = num_blocks * page;
+    q.cache = static_cast<__nv_bfloat16*>(cache);
+    q.sblk = stride_block;
+    q.stok = stride_tok;
+    q.page = page;
+    q.W = row_width;
+    q.lk = lk;
+    q.T = static_cast<int>(num_tokens);
+    q.G = belt::kG;
+    q.eps = eps;
+    q.vec_ok = aligned16(cache) && stride_tok % 8 == 0 && stride_block % 8 == 0;
+    q.c = static_cast<const __nv_bfloat16*>(c);
+    q.sct = c_st;
+    q.c_in = 1;
+    q.c_vec = aligned16(c) && c_st % 8 == 0;
+    if (pw_items(q, k_segs, lk, row_width, "latent_rows_to_cache") == BELT_OK) {
+      belt::ProjWriteMaps maps{};
+      cuuint64_t dims[2] = {static_cast<cuuint64_t>(belt::kG * belt::kD), static_cast<cuuint64_t>(lk)};
+      cuuint64_t strides[1] = {static_cast<cuuint64_t>(belt::kG * belt::kD) * 2};
+      cuuint32_t box[2] = {64, 64};
+      int r = encode_bf16(&maps.u, u_cat, 2, dims, strides, box, "u_cat");
+      if (r != BELT_OK) return r;
+      cudaError_t e = belt::launch_proj_write(maps, q, as_stream(stream));
+      return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
+    }
   }
   cudaError_t e = belt::launch_cache_write(p, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
@@ -307,46 +384,10 @@ int belt_latent_proj_rows_to_cache(const void* x, int64_t num_tokens, int64_t x_
   p.eps = eps;
   p.vec_ok = aligned16(cache) && stride_tok % 8 == 0 && stride_block % 8 == 0;
   p.err = err;
-  // work items: every group's 64-column window, then the V part [lk, W) in windows of four chunks
-  int items = 0;
-  for (int g = 0; g < belt::kG; ++g) {
-    p.a_lo[g] = k_segs[4 * g];
-    p.a_n[g] = k_segs[4 * g + 1];
-    p.b_lo[g] = k_segs[4 * g + 2];
-    p.b_n[g] = k_segs[4 * g + 3];
-    const int r = p.a_n[g] + p.b_n[g];
-    if (p.a_lo[g] < 0 || p.b_lo[g] < 0 || p.a_n[g] < 0 || p.b_n[g] < 0 || r > 256 ||
-        p.a_lo[g] + p.a_n[g] > lk || (p.b_n[g] > 0 && p.b_lo[g] + p.b_n[g] > lk))
-      return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: k_segs of group %d out of range (lk %d)", g, lk);
-    bool use[64] = {};
-    const int runs[2][2] = {{p.a_lo[g], p.a_n[g]}, {p.b_lo[g], p.b_n[g]}};
-    for (int q = 0; q < 2; ++q)
-      if (runs[q][1] > 0)
-        for (int c = runs[q][0] >> 6; c <= (runs[q][0] + runs[q][1] - 1) >> 6 && c < 64; ++c) use[c] = true;
-    int n = 0;
-    for (int c = 0; c < 64; ++c)
-      if (use[c]) {
-        if (n == belt::kPwMaxChunks)
-          return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: group %d spans more than %d 64-column chunks", g,
-                      belt::kPwMaxChunks);
-        p.item_chunk[items][n++] = c;
-      }
-    if (n == 0) {   // a group without coordinates still gets an item (nothing to write); keep one chunk to stream
-      p.item_chunk[items][0] = 0;
-      n = 1;
-    }
-    p.item_nch[items++] = n;
+  {
+    const int r = pw_items(p, k_segs, lk, row_width, "latent_proj_rows_to_cache");
+    if (r != BELT_OK) return r;
   }
-  // V part in windows of two 64-column chunks: more CTAs, each streaming a smaller share of W_down
-  constexpr int kVChunks = 2;
-  for (int c = lk >> 6; c < (row_width + 63) >> 6; c += kVChunks) {
-    if (items == belt::kPwMaxItems)
-      return fail(BELT_ERR_INVALID, "latent_proj_rows_to_cache: V part too wide (%d columns)", row_width - lk);
-    const int n = ((row_width + 63) >> 6) - c < kVChunks ? ((row_width + 63) >> 6) - c : kVChunks;
-    for (int i = 0; i < n; ++i) p.item_chunk[items][i] = c + i;
-    p.item_nch[items++] = n;
-  }
-  p.n_items = items;
   belt::ProjWriteMaps maps;
   {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(num_tokens)};

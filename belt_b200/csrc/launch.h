@@ -159,6 +159,11 @@ struct ProjWriteParams {
   float eps;
   int vec_ok;   // cache rows 16-byte aligned
   int* err;
+  // c-input mode (latent_rows_to_cache): the latent rows come from c [T, >= W] (row stride sct elements) instead of
+  // x W_down^T; maps.x / maps.w are then unused. c_vec: c rows 16-byte aligned.
+  const __nv_bfloat16* c;
+  long long sct;
+  int c_in, c_vec;
 };
 cudaError_t launch_proj_write(const ProjWriteMaps& maps, const ProjWriteParams& p, cudaStream_t stream);
 

@@ -16,6 +16,9 @@
 //   phase 2 (groups): k_pre[token, channel] = c_window . u_cat[window rows, g*256 + channel] (N = 256, u_cat read
 //            MN-major; rows of other groups meet zeros in A, rows past lk are zero-filled by TMA);
 //   epilogue 2: rho from the 256 channels, the group's runs scaled and written to the cache row.
+// In c-input mode (``latent_rows_to_cache``, latent_ops.py:138-158: the model computed c) phase 1 is skipped and
+// epilogue 1 reads the window columns of c from global memory; phase 2 and epilogue 2 are the same, so the RMS fold
+// runs on the tensor cores at every batch size.
 #include "common.cuh"
 #include "launch.h"
 
@@ -74,8 +77,10 @@ __global__ void __launch_bounds__(kPwThreads, 1)
     for (int i = 0; i < kPwBars; ++i) mbar_init(&bars[i], i == pA2 ? kPwThreads : 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&maps.x);
-    tma_prefetch_desc(&maps.w);
+    if (!p.c_in) {
+      tma_prefetch_desc(&maps.x);
+      tma_prefetch_desc(&maps.w);
+    }
     tma_prefetch_desc(&maps.u);
   }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
@@ -88,7 +93,9 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   const uint32_t base = smem_u32(smem);
 
   // ------------------------------------------------------------------ phase 1 (roles)
-  if (threadIdx.x == 0) {
+  if (p.c_in) {
+    // c is given: nothing to compute
+  } else if (threadIdx.x == 0) {
     int issued = 0;
     for (int k = 0; k < nk; ++k) {
       const int s = k % kPwStages;
@@ -135,7 +142,8 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   }
   __syncwarp();
 
-  const bool done1 = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[pDone1], 0, p.err, kErrTimeoutEpilogue));
+  const bool done1 =
+      p.c_in || __all_sync(0xffffffffu, mbar_wait_bounded(&bars[pDone1], 0, p.err, kErrTimeoutEpilogue));
   tc_fence_after();
   const bool live = done1 && !*abort_flag;
   // phase-2 operands for the first two chunks can stream in while epilogue 1 runs (the ring is free now)
@@ -150,24 +158,56 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   }
 
   __syncwarp();
-  // ------------------------------------------------------------------ epilogue 1: c = bf16(D1)
+  // ------------------------------------------------------------------ epilogue 1: c = bf16(D1), or c itself
+  const __nv_bfloat16* crow = p.c_in && row < p.T ? p.c + static_cast<long long>(row) * p.sct : nullptr;
   if (live) {
     for (int i = 0; i < nch; ++i) {
       const int col0 = 64 * p.item_chunk[item][i];
       uint32_t v[32];
       for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem + lane_base + 64 * i + 32 * half, v);
-        tmem_ld_wait();
         uint32_t pk[16];
+        const int cb = col0 + 32 * half;
+        if (p.c_in) {
+          // 32 columns of this token's c row (zeros past W or past the last token)
+          if (crow && p.c_vec && cb + 32 <= p.W) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
-          if (group) {
-            const int c = col0 + 32 * half + 2 * j;
-            if (!in_runs(c)) lo = 0.f;
-            if (!in_runs(c + 1)) hi = 0.f;
+            for (int u = 0; u < 4; ++u) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(crow + cb + 8 * u));
+              pk[4 * u] = w.x;
+              pk[4 * u + 1] = w.y;
+              pk[4 * u + 2] = w.z;
+              pk[4 * u + 3] = w.w;
+            }
+          } else {
+            const uint16_t* cr = reinterpret_cast<const uint16_t*>(crow);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t lo = crow && cb + 2 * j < p.W ? cr[cb + 2 * j] : 0u;
+              const uint32_t hi = crow && cb + 2 * j + 1 < p.W ? cr[cb + 2 * j + 1] : 0u;
+              pk[j] = lo | (hi << 16);
+            }
           }
-          pk[j] = pack_bf16(lo, hi);
+          if (group) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int c = cb + 2 * j;
+              if (!in_runs(c)) pk[j] &= 0xFFFF0000u;
+              if (!in_runs(c + 1)) pk[j] &= 0x0000FFFFu;
+            }
+          }
+        } else {
+          tmem_ld32(tmem + lane_base + 64 * i + 32 * half, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
+            if (group) {
+              const int c = cb + 2 * j;
+              if (!in_runs(c)) lo = 0.f;
+              if (!in_runs(c + 1)) hi = 0.f;
+            }
+            pk[j] = pack_bf16(lo, hi);
+          }
         }
         if (group) {
           uint8_t* a2 = smem + kPwA2 + i * kPwXBytes;

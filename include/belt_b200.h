@@ -81,6 +81,8 @@ int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_s
  * s < 0 or s >= num_blocks * page is skipped. cache: the layer's [num_blocks, page, W] BF16 view with element
  * strides (stride_block, stride_tok, 1). u_cat [lk, 4 * 256] BF16 contiguous; k_segs: host int32 [4][4] =
  * (start, length, start, length) per group; eps of the k_norm RMS. Writes rows [c_K / rho | c[lk:W]].
+ * The RMS fold runs on the tensor cores whenever every group lies within five 64-column chunks and u_cat is 16-byte
+ * aligned (a SIMT kernel otherwise); the results agree within one BF16 ulp either way.
  */
 int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, const void* slots, int32_t slots_i64,
                               void* cache, int64_t num_blocks, int32_t page, int32_t row_width, int64_t stride_block,

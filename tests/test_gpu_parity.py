@@ -148,6 +148,40 @@ def test_cache_write_strided_view_and_padding():
     assert not full[:, 0].any() and not full[:, 2].any()          # neighbouring layers untouched
 
 
+def test_cache_write_prefill_chunk_and_unaligned_inputs():
+    """The cache write at prefill size (an 8192-token chunk, sampled against the oracle; the tensor-core fold), with c
+    rows that are not 16-byte aligned (element loads), and with a u_cat that is not 16-byte aligned (the SIMT
+    kernel). Values within 1 BF16 ulp, rows never written left zero."""
+    spec = synth.c50()
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w)
+    W = w.layout["row_width"]
+    page = 16
+    g = torch.Generator().manual_seed(31)
+    cols = torch.cat([synth.latent_columns(w.layout), torch.ones(8)])
+    u_off = torch.empty(lat.u_cat.numel() + 1, dtype=torch.bfloat16, device=DEV)[1:].view_as(lat.u_cat)
+    u_off.copy_(lat.u_cat)
+    for T, c_off, u_cat in ((8192, 0, lat.u_cat), (300, 1, lat.u_cat), (300, 0, u_off)):
+        nb = T // page + 8
+        c_full = (torch.randn(T, W + 8, generator=g) * cols).to(torch.bfloat16)
+        c = c_full[:, c_off:c_off + W]
+        slots = torch.randperm(nb * page, generator=g)[:T]
+        slots[::11] = -1
+        cache = torch.zeros(nb, page, W, dtype=torch.bfloat16, device=DEV)
+        c_dev = c_full.to(DEV)[:, c_off:c_off + W]
+        latent_ops.latent_rows_to_cache(c_dev, slots.to(DEV), cache, u_cat, lat.k_segs, 1e-6)
+        torch.cuda.synchronize()
+        live = torch.nonzero(slots >= 0).flatten()
+        sample = live[torch.randperm(live.numel(), generator=g)[:256]]
+        exp = oracle.latent_rows(c[sample], slots[sample], torch.zeros(nb, page, W, dtype=torch.bfloat16),
+                                 ref["u_cat"], ref["k_segs"], 1e-6)
+        got = cache.cpu().view(-1, W)
+        assert bf16_ulp_close(got[slots[sample]], exp.view(-1, W)[slots[sample]], ulps=1), (T, c_off)
+        written = torch.zeros(nb * page, dtype=torch.bool)
+        written[slots[slots >= 0]] = True
+        assert not got[~written].any(), (T, c_off)
+
+
 # ------------------------------------------------------------------------------------------------- fused down-projection
 # The kernel rounds c = x W_down^T to BF16 after an FP32 sum over `hidden` terms in another order than the oracle's
 # (the reference's own cuBLAS linear has the same freedom). An element of c can then sit one BF16 ulp away, and the
