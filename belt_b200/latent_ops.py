@@ -111,11 +111,18 @@ def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: tor
               _stream_ptr(c.device))
 
 
+# From this many tokens on (prefill chunks) the projection runs as a library GEMM followed by the cache write: the fused
+# kernel re-streams W_down for every 128 tokens, which costs more than the round trip of c (8192 tokens: 52 against
+# 66 us); below it the fused kernel is as fast and needs no buffer for c.
+FUSED_WRITE_MAX_TOKENS = 2048
+
+
 def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor,
-                          u_cat: torch.Tensor, k_segs, eps: float) -> None:
-    """``latent_rows_to_cache(bf16(x @ w_down^T), ...)`` in one kernel: x [T, hidden] BF16 (the layer inputs of the new
-    tokens), w_down [>= W, hidden] BF16 (``kv_latent_proj.weight``, zero rows at the gaps), the other arguments as
-    ``latent_rows_to_cache``. The latent projection itself is never materialised."""
+                          u_cat: torch.Tensor, k_segs, eps: float, fused: bool | None = None) -> None:
+    """``latent_rows_to_cache(bf16(x @ w_down^T), ...)``: x [T, hidden] BF16 (the layer inputs of the new tokens),
+    w_down [>= W, hidden] BF16 (``kv_latent_proj.weight``, zero rows at the gaps), the other arguments as
+    ``latent_rows_to_cache``. ``fused`` (default: fewer than FUSED_WRITE_MAX_TOKENS tokens) runs it as one kernel that
+    never materialises the projection; otherwise the projection is a library GEMM into a [T, W] buffer."""
     T = slot_mapping.shape[0]
     if T == 0:
         return
@@ -131,6 +138,11 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
         raise ValueError("project_rows_to_cache: x [T, hidden], w_down [>= W, hidden], contiguous u_cat")
     if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous():
         raise ValueError("project_rows_to_cache: contiguous int32 / int64 slot_mapping")
+    if fused is None:
+        fused = T < FUSED_WRITE_MAX_TOKENS
+    if not fused:
+        latent_rows_to_cache(x[:T] @ w_down[:W].T, slot_mapping, cache, u_cat, k_segs, eps)
+        return
     from .decode import error_word
     _lib.call("belt_latent_proj_rows_to_cache", x.data_ptr(), T, x.stride(0), x.shape[1], w_down.data_ptr(),
               w_down.stride(0), slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), cache.data_ptr(),

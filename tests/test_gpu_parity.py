@@ -242,8 +242,10 @@ def test_proj_write_strided_view_multi_tile():
     assert not full[:, 0].any() and not full[:, 2].any()
 
 
-def test_proj_write_prefill_chunk():
-    """An 8192-token chunk (the chunked-prefill write), checked on a sample of 256 tokens against the oracle."""
+@pytest.mark.parametrize("fused", [True, False])
+def test_proj_write_prefill_chunk(fused):
+    """An 8192-token chunk (the chunked-prefill write), checked on a sample of 256 tokens against the oracle: through the
+    fused kernel, and as a library GEMM + the cache write (the default at this size)."""
     spec = synth.c50()
     w = synth.make_layer(spec)
     lat, ref = layer_pair(w)
@@ -255,7 +257,7 @@ def test_proj_write_prefill_chunk():
     slots = torch.randperm(nb * page, generator=g)[:T]
     cache = torch.zeros(nb, page, W, dtype=torch.bfloat16, device=DEV)
     latent_ops.project_rows_to_cache(x.to(DEV), w.kv_latent_proj.to(DEV), slots.to(DEV), cache, lat.u_cat,
-                                     lat.k_segs, 1e-6)
+                                     lat.k_segs, 1e-6, fused=fused)
     torch.cuda.synchronize()
     dec.check_device_errors(DEV)
     sample = torch.randperm(T, generator=g)[:256]
