@@ -1,7 +1,7 @@
 """belt_b200: the latent-KV decode hot path of BELT, written for B200 (sm_100a).
 
 Modules:
-  export_latent   the latent export format (row layout, column runs, RoPE change of basis, tensors)
+  latent_format   the latent export directory: reader (``load_latent_layers``), writer, row layout
   layer           ``LatentLayer`` and ``derive_latent_tensors`` (load-time constants)
   decode          split-KV schedule, decode kernel, segment merge (``vllm_lrkv.cute_decode`` surface)
   latent_ops      absorbed query, V up-projection, cache write (``vllm_lrkv.latent_ops`` surface)

@@ -18,8 +18,8 @@ c_i32p = ctypes.POINTER(ctypes.c_int32)
 SIGNATURES = {
     "belt_decode_schedule": [c_vp, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
     "belt_decode_schedule_weighted": [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
-    "belt_block_diag_query": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32p, c_vp, c_vp],
-    "belt_up_project": [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp],
+    "belt_block_diag_query": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32p, c_vp, c_vp, c_vp],
+    "belt_up_project": [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
     "belt_latent_rows_to_cache": [c_vp, c_i64, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp,
                                   c_i32, c_i32p, c_f32, c_vp],
     "belt_latent_proj_rows_to_cache": [c_vp, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32,

@@ -67,7 +67,7 @@ cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Out = X W per head's group (block_diag_query, up_project): on the tensor cores when TMA can describe X and W
 // (16-byte aligned bases and strides, W rows contiguous), else on the SIMT kernel.
-int run_group_product(const belt::GroupGemmParams& gp, const char* what, cudaStream_t stream) {
+int run_group_product(const belt::GroupGemmParams& gp, const char* what, int32_t* err, cudaStream_t stream) {
   const bool tma_ok = aligned16(gp.X) && aligned16(gp.W) && gp.swn == 1 && gp.sxh > 0 && gp.sxt > 0 &&
                       (gp.sxh * 2) % 16 == 0 && (gp.sxt * 2) % 16 == 0 && (gp.swk * 2) % 16 == 0 &&
                       (gp.swg * 2) % 16 == 0 && gp.K > 0 && gp.sxh >= gp.K &&
@@ -112,7 +112,7 @@ int run_group_product(const belt::GroupGemmParams& gp, const char* what, cudaStr
     // 64 for the 256-column U_v projection (more CTAs for its deeper K loop)
     hp.nb = gp.N <= 256 ? 1 : 2;
     hp.vec_out = aligned16(gp.Out) && gp.sot % 8 == 0 && gp.soh % 8 == 0;
-    hp.err = nullptr;
+    hp.err = err;
     e = belt::launch_head_gemm(maps, hp, stream);
   } else {
     e = belt::launch_group_gemm(gp, stream);
@@ -133,7 +133,7 @@ extern "C" {
 
 const char* belt_last_error(void) { return g_last_error.c_str(); }
 
-int belt_abi_version(void) { return 100; }
+int belt_abi_version(void) { return 200; }
 
 int belt_num_sms(int32_t device) {
   int n = 0;
@@ -173,7 +173,7 @@ int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int
 }
 
 int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64_t q_sh, const void* qmap,
-                          int32_t kq, const int32_t* col_runs, void* q_bd, void* stream) {
+                          int32_t kq, const int32_t* col_runs, void* q_bd, int32_t* err, void* stream) {
   if (num_tokens < 0 || kq <= 0 || !col_runs) return fail(BELT_ERR_INVALID, "block_diag_query: bad arguments");
   if (num_tokens == 0) return ok();
   if (!q || !qmap || !q_bd) return fail(BELT_ERR_INVALID, "block_diag_query: null buffer");
@@ -202,12 +202,12 @@ int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64
       p.run_hi[g][i] = hi;
     }
   }
-  const int r = run_group_product(p, "block_diag_query", as_stream(stream));
+  const int r = run_group_product(p, "block_diag_query", err, as_stream(stream));
   return r == BELT_OK ? ok() : r;
 }
 
 int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_sh, int32_t r_v, const void* v_up_t,
-                    void* out, int64_t out_st, int64_t out_sh, void* stream) {
+                    void* out, int64_t out_st, int64_t out_sh, int32_t* err, void* stream) {
   if (num_tokens < 0 || r_v <= 0) return fail(BELT_ERR_INVALID, "up_project: bad arguments");
   if (num_tokens == 0) return ok();
   if (!a || !v_up_t || !out) return fail(BELT_ERR_INVALID, "up_project: null buffer");
@@ -232,7 +232,7 @@ int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_s
     p.run_lo[g][0] = 0;
     p.run_hi[g][0] = belt::kD;
   }
-  const int r = run_group_product(p, "up_project", as_stream(stream));
+  const int r = run_group_product(p, "up_project", err, as_stream(stream));
   return r == BELT_OK ? ok() : r;
 }
 

@@ -9,7 +9,7 @@
 //
 // The array holds kScratchBytes (24 MiB) on every GPU that loads the library, from the load until the process exits.
 // Limits that follow from it, checked before anything runs: num_reqs <= kMaxReqs, num_ctas <= kMaxCtas, and
-// (num_reqs + num_ctas) * 24 * (lv + 1) * 4 bytes of partials <= kPartBytes (at lv = 640 and 148 CTAs: 259 requests).
+// (num_reqs + num_ctas) * 24 * (lv + 1) * 4 bytes of partials <= kPartBytes (at lv = 640 and 148 CTAs: 258 requests).
 //
 // Every call on a device uses the same array and leaves its contents there for the next call. No byte of it has to
 // start at zero: the schedule writes every segment record, CTA range and request range that the decode and the merge
@@ -17,9 +17,15 @@
 // (different streams of one device without an ordering between them, or several host threads on one device) race on
 // the array and give wrong results; calls on one stream run one after the other.
 //
-// The array's device address is looked up once per device, by the first call made while that device is current
-// (cudaGetSymbolAddress, which can make the CUDA runtime load this library's device code on that device). Make that
-// first call before any stream capture begins.
+// The split is the cost-weighted one the backend uses (belt_decode_schedule_weighted, start cost kStartCost): same
+// outputs as the reference's equal-tiles split within the decode's tolerance, about 2.5 % less decode time.
+//
+// Where the array is: its device address belongs to the CUDA context that loaded this library's device code. Every
+// call made outside stream capture looks it up again (cudaGetSymbolAddress, which can make the runtime load the
+// device code in that context) and records it for the current context; a call made while `stream` is capturing uses
+// the record of the current context and is refused if there is none. So the first call in a context (the first on a
+// device, the first under a driver-API context a host made current, and the first after a cudaDeviceReset, which
+// loads the device code again, possibly at another address) must come before any stream capture begins.
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -27,6 +33,7 @@
 #include "../../include/belt_b200.h"
 #include "common.cuh"
 #include "launch.h"
+#include "scratch_cache.h"
 
 // The host-side name stands for the array; its device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_decode_scratch[24u << 20];
@@ -36,7 +43,8 @@ namespace {
 constexpr size_t kScratchBytes = sizeof(g_decode_scratch);
 constexpr int kMaxReqs = 4096;
 constexpr int kMaxCtas = 1024;
-constexpr int kMaxDevices = 64;
+constexpr int kStartCost = 10;     // the backend's weighted split (extra cost of a request's first tile)
+constexpr int kCacheSlots = 64;    // contexts remembered (oldest dropped beyond this)
 // Schedule records at fixed offsets, then the partials.
 constexpr size_t kWorkOff = 0;                                                   // [(kMaxReqs + kMaxCtas), 4] int32
 constexpr size_t kCtaSegOff = kWorkOff + size_t(kMaxReqs + kMaxCtas) * 4 * 4;    // [kMaxCtas + 1] int32
@@ -46,7 +54,7 @@ constexpr size_t kPartBytes = kScratchBytes - kPartOff;
 static_assert(kSegBaseOff + size_t(kMaxReqs + 1) * 4 <= kPartOff, "schedule records overlap the partials");
 
 std::mutex g_mu;
-unsigned char* g_scratch_ptr[kMaxDevices] = {};
+belt::ScratchAddressCache<kCacheSlots> g_scratch;
 
 // Records the failure for belt_last_error() and returns `code`.
 int reject(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
@@ -60,24 +68,56 @@ int reject(int code, const char* fmt, ...) {
   return code;
 }
 
-// Device address of the scratch array on the current device; the lookup runs once per device.
-int scratch_on_current_device(unsigned char** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The calling thread's current driver context (the runtime's primary context of the current device, or a context a
+// driver-API host made current), through the driver entry point the runtime exposes (no link against libcuda).
+int current_context(CUcontext* ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return reject(BELT_ERR_CUDA, "latent_decode_noalloc: cuCtxGetCurrent is unavailable");
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  if (fn(ctx) != CUDA_SUCCESS || !*ctx) return reject(BELT_ERR_CUDA, "latent_decode_noalloc: no current CUDA context");
+  return BELT_OK;
+}
+
+// Device address of the scratch array in the current context: looked up again outside stream capture, taken from the
+// record of this context while `stream` captures.
+int scratch_in_current_context(cudaStream_t stream, unsigned char** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return reject(BELT_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return reject(BELT_ERR_CUDA, "device %d beyond %d devices", dev, kMaxDevices);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  const bool capturing = cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* ptr = nullptr;
+  void* ptr = nullptr;
+  CUcontext ctx = nullptr;
+  if (capturing) {
+    const int r = current_context(&ctx);
+    if (r != BELT_OK) return r;
+    ptr = g_scratch.find(ctx);
+    if (!ptr)
+      return reject(BELT_ERR_INVALID,
+                    "latent_decode_noalloc: first call in this CUDA context (device %d) made during stream capture; "
+                    "make one call outside capture first", dev);
+  } else {
     e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
     if (e != cudaSuccess)
       return reject(BELT_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s (%s)", dev, cudaGetErrorString(e),
                     cudaGetErrorName(e));
     if (!ptr || (reinterpret_cast<uintptr_t>(ptr) & 255u))
       return reject(BELT_ERR_CUDA, "scratch array on device %d is not 256-byte aligned", dev);
-    g_scratch_ptr[dev] = static_cast<unsigned char*>(ptr);
+    // the lookup made the context current if it was not yet (the runtime's primary context of `dev`)
+    const int r = current_context(&ctx);
+    if (r != BELT_OK) return r;
+    g_scratch.refresh(ctx, ptr);
   }
-  *out = g_scratch_ptr[dev];
+  *out = static_cast<unsigned char*>(ptr);
   return BELT_OK;
 }
 
@@ -118,15 +158,15 @@ int belt_latent_decode_noalloc(const void* q_bd, int32_t num_reqs, int32_t kq, c
   if (!out || !lse || !seq_lens) return reject(BELT_ERR_INVALID, "latent_decode_noalloc: null buffer");
 
   unsigned char* base = nullptr;
-  int r = scratch_on_current_device(&base);
+  int r = scratch_in_current_context(reinterpret_cast<cudaStream_t>(stream), &base);
   if (r != BELT_OK) return r;
   int32_t* work = reinterpret_cast<int32_t*>(base + kWorkOff);
   int32_t* cta_seg = reinterpret_cast<int32_t*>(base + kCtaSegOff);
   int32_t* seg_base = reinterpret_cast<int32_t*>(base + kSegBaseOff);
   float* part = reinterpret_cast<float*>(base + kPartOff);
 
-  r = belt_decode_schedule(seq_lens, num_reqs, num_ctas, min_tiles, work, static_cast<int64_t>(num_reqs) + num_ctas,
-                           cta_seg, seg_base, err, stream);
+  r = belt_decode_schedule_weighted(seq_lens, num_reqs, num_ctas, min_tiles, kStartCost, work,
+                                    static_cast<int64_t>(num_reqs) + num_ctas, cta_seg, seg_base, err, stream);
   if (r != BELT_OK) return forward(r, "latent_decode_noalloc");
   r = belt_latent_decode(q_bd, num_reqs, kq, cache, num_blocks, page, row_width, stride_block, stride_tok, block_table,
                          bt_stride, seq_lens, work, cta_seg, num_ctas, part, part_ss, part_sh, sm_scale, lk_pad, lv,

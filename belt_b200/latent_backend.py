@@ -117,6 +117,46 @@ class LatentAttentionMetadata:
 _LAST_BUILD: dict = {}
 _SCHEDULES: dict = {}
 _SIDE_STREAMS: dict = {}
+_ERROR_WATCHES: dict = {}
+
+
+class _ErrorWatch:
+    """Reads a device's error word (``decode.error_word``) one step late, without a synchronisation: every build
+    enqueues a copy of the word into pinned host memory behind the work already queued, and the next build reads that
+    copy if it has landed (otherwise the check waits for a later build). A nonzero word means a bounded wait inside a
+    kernel gave up on an earlier step, so that step's output is not valid: the build raises ``BeltError`` (and clears
+    the word). Nothing is enqueued or read while the stream is capturing a CUDA graph."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.landed = torch.cuda.Event()
+        self.armed = False
+
+    def poll(self) -> None:
+        if torch.cuda.is_current_stream_capturing():
+            return
+        if self.armed:
+            if not self.landed.query():
+                return                              # the GPU is still behind: read at a later build
+            self.armed = False
+            code = int(self.host[0])
+            if code:
+                dec.error_word(self.device).zero_()
+                from ._lib import BeltError
+                raise BeltError(f"device error 0x{code:x} recorded by a belt kernel on {self.device} in an earlier "
+                                "step: its attention output is not valid")
+        stream = torch.cuda.current_stream(self.device)
+        self.host.copy_(dec.error_word(self.device), non_blocking=True)
+        self.landed.record(stream)
+        self.armed = True
+
+
+def _error_watch(device: torch.device) -> _ErrorWatch:
+    w = _ERROR_WATCHES.get(device)
+    if w is None:
+        w = _ERROR_WATCHES[device] = _ErrorWatch(device)
+    return w
 
 
 def _side_stream(device: torch.device) -> torch.cuda.Stream:
@@ -170,6 +210,7 @@ class LatentAttentionMetadataBuilder:
         return m
 
     def _build(self, cm: CommonAttentionMetadata) -> LatentAttentionMetadata:
+        _error_watch(self.device).poll()
         nd, npf, ndt, npt = split_decodes_and_prefills(cm, decode_threshold=1)
         m = LatentAttentionMetadata(num_actual_tokens=cm.num_actual_tokens, num_decodes=nd, num_decode_tokens=ndt,
                                     num_prefills=npf, num_prefill_tokens=npt, block_table=cm.block_table_tensor,

@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .decode import _stream_ptr
+from .decode import _stream_ptr, error_word
 
 HEAD_DIM = 256
 
@@ -63,7 +63,7 @@ def block_diag_query(q: torch.Tensor, qmap: torch.Tensor, col_runs=None) -> torc
     runs = col_runs if col_runs is not None else _runs_dense(KQ)
     flat = [x for g in runs for r in g for x in r]
     _lib.call("belt_block_diag_query", q.data_ptr(), T, q.stride(0), q.stride(1), qmap.data_ptr(), KQ,
-              _lib.int_array(flat), out.data_ptr(), _stream_ptr(q.device))
+              _lib.int_array(flat), out.data_ptr(), error_word(q.device).data_ptr(), _stream_ptr(q.device))
     return out
 
 
@@ -78,7 +78,7 @@ def up_project(a: torch.Tensor, v_up_t: torch.Tensor, out: torch.Tensor) -> None
     if a.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or v_up_t.dtype != torch.bfloat16:
         raise ValueError("up_project: BF16 tensors")
     _lib.call("belt_up_project", a.data_ptr(), a.shape[0], a.stride(0), a.stride(1), R, v_up_t.data_ptr(),
-              out.data_ptr(), out.stride(0), out.stride(1), _stream_ptr(a.device))
+              out.data_ptr(), out.stride(0), out.stride(1), error_word(a.device).data_ptr(), _stream_ptr(a.device))
 
 
 def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor, u_cat: torch.Tensor,
@@ -143,7 +143,6 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
     if not fused:
         latent_rows_to_cache(x[:T] @ w_down[:W].T, slot_mapping, cache, u_cat, k_segs, eps)
         return
-    from .decode import error_word
     _lib.call("belt_latent_proj_rows_to_cache", x.data_ptr(), T, x.stride(0), x.shape[1], w_down.data_ptr(),
               w_down.stride(0), slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), cache.data_ptr(),
               cache.shape[0], cache.shape[1], W, cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk,
@@ -175,7 +174,6 @@ def decompress_paged(cache: torch.Tensor, block_table_row: torch.Tensor, seq_len
             raise ValueError(f"decompress_paged: {name} [count, 4, 256] BF16 with contiguous channels")
     if k_out.stride() != v_out.stride():
         raise ValueError("decompress_paged: k_out and v_out with the same strides")
-    from .decode import error_word
     _lib.call("belt_latent_decompress", cache.data_ptr(), cache.shape[0], cache.shape[1], cache.shape[2],
               cache.stride(0), cache.stride(1), block_table_row.data_ptr(), int(seq_len), int(pos0), int(count),
               wk.data_ptr(), kc, _lib.int_array(host_k_segs(k_segs)), v_up_t.data_ptr(), int(v_offset), r_v,
@@ -206,7 +204,6 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos0:
         raise ValueError("prefill_attention: q [ql, 24, 256], k / v [S, 4, 256] with equal strides, out like q")
     if lse.dtype != torch.float32 or tuple(lse.shape) != (ql, H) or lse.stride(1) != 1:
         raise ValueError("prefill_attention: lse [ql, 24] fp32 with contiguous heads")
-    from .decode import error_word
     _lib.call("belt_prefill_attention", q.data_ptr(), ql, q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), S,
               k.stride(0), k.stride(1), int(q_pos0), int(k_pos0), int(bool(causal)), float(scale), out.data_ptr(),
               out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), error_word(dev).data_ptr(),

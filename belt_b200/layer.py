@@ -91,7 +91,7 @@ def derive_latent_tensors(k_up: torch.Tensor, v_up: torch.Tensor, k_norm_weight:
     """``LatentLayer`` of one compressed layer from its export tensors (qwen3_5_latent.py:161-202).
 
     k_up [G, D, r_max], v_up [G * D, r_v] (BF16, as loaded), k_norm_weight [D] (zero-centred RMSNorm weight: the
-    gain is 1 + weight), ``layout`` (``export_latent.row_layout``), cos_sin_cache [max_pos, rot] (the rotary
+    gain is 1 + weight), ``layout`` (``latent_format.row_layout``: the kv_lowrank entry of the layer), cos_sin_cache [max_pos, rot] (the rotary
     embedding's table, any float dtype; stored BF16)."""
     device = torch.device(device) if device is not None else k_up.device
     k_up = k_up.detach().to("cpu")

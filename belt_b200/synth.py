@@ -6,7 +6,7 @@ here from fixed seeds with the shapes and distributions the benchmark configurat
 * geometry of one compressed full-attention layer: 24 query heads in 4 KV groups, head_dim 256, partial NeoX RoPE on
   the first 64 channels, theta 1e7;
 * factors per group U_g [256, r_g] ~ N(0, 1/r_g), U_v [4 * 256, r_v] ~ N(0, 1/r_v), down-projections
-  VS [r, hidden] ~ N(0, 1/hidden), passed through the export's change of basis (``export_latent.build_latent_layer``);
+  VS [r, hidden] ~ N(0, 1/hidden), passed through the export's change of basis (``latent_format.latent_tensors``);
 * cache rows ~ N(0, 1) in every latent column, zero in the alignment gaps; physical blocks dealt to requests by a
   seeded random permutation; blocks no request owns are NaN-poisoned so a stray read shows up;
 * queries ~ N(0, 1) BF16; token t of a request sits at position t.
@@ -21,7 +21,7 @@ import math
 
 import torch
 
-from . import export_latent
+from . import latent_format
 
 H, G, D, ROT = 24, 4, 256, 64
 THETA = 1e7
@@ -40,8 +40,7 @@ class LayerSpec:
 
     @property
     def row_width(self) -> int:
-        return export_latent.row_layout(list(self.k_ranks), self.v_rank, G, ROT, rope_align=self.rope_align)[
-            "row_width"]
+        return latent_format.row_layout(self.k_ranks, self.v_rank, ROT, rope_align=self.rope_align)["row_width"]
 
 
 def c50(hidden: int = 1024, **kw) -> LayerSpec:
@@ -89,7 +88,7 @@ def make_factors(spec: LayerSpec, seed: int = SEED_FACTORS):
 
 @dataclass
 class LayerWeights:
-    """What a latent export holds for one compressed layer (``export_latent.build_latent_layer``)."""
+    """What a latent export holds for one compressed layer (``latent_format.latent_tensors``)."""
 
     kv_latent_proj: torch.Tensor      # [pe_offset, hidden] BF16
     k_up: torch.Tensor                # [G, D, r_max] BF16
@@ -100,17 +99,13 @@ class LayerWeights:
 
 def make_layer(spec: LayerSpec, seed: int = SEED_FACTORS) -> LayerWeights:
     k_blocks, v_factors, k_norm = make_factors(spec, seed)
-    proj, k_up, v_up, layout = export_latent.build_latent_layer(k_blocks, v_factors, G, D, ROT,
-                                                                rope_align=spec.rope_align)
+    proj, k_up, v_up, layout = latent_format.latent_tensors(k_blocks, v_factors, D, ROT, rope_align=spec.rope_align)
     return LayerWeights(proj, k_up, v_up, k_norm, layout)
 
 
 def cos_sin_table(max_pos: int, rotary_dim: int = ROT, theta: float = THETA) -> torch.Tensor:
     """The model's NeoX cos/sin cache [max_pos, rot] in fp32 (cos half | sin half), computed on the CPU."""
-    inv_freq = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.float) / rotary_dim))
-    t = torch.arange(max_pos, dtype=torch.float)
-    freqs = torch.einsum("i,j -> ij", t, inv_freq)
-    return torch.cat((freqs.cos(), freqs.sin()), dim=-1)
+    return latent_format.cos_sin_table(max_pos, rotary_dim, theta)
 
 
 @dataclass

@@ -29,7 +29,7 @@ extern "C" {
 /* Thread-local description of the last failure of a belt_* call on this thread ("" if none). */
 const char* belt_last_error(void);
 
-/* ABI version of this library (major * 100 + minor). */
+/* ABI version of this library (major * 100 + minor). 200: the per-head GEMM entry points take an error word. */
 int belt_abi_version(void);
 
 /*
@@ -61,18 +61,19 @@ int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int
  * (contiguous) -> q_bd [T, 24, kq] BF16 (contiguous). Only the columns listed in col_runs are computed for each
  * group (host array [4][3][2] of [start, end) runs, an empty run has start == end); the other columns are written
  * as zeros. A qmap made by `derive_latent_tensors` is zero outside its group's latent columns and RoPE chunk, so
- * passing those runs gives the dense product.
+ * passing those runs gives the dense product. err: optional device int32 word that receives a nonzero code if a
+ * bounded wait in the tensor-core kernel timed out (the output is then not valid).
  */
 int belt_block_diag_query(const void* q, int64_t num_tokens, int64_t q_st, int64_t q_sh, const void* qmap,
-                          int32_t kq, const int32_t* col_runs, void* q_bd, void* stream);
+                          int32_t kq, const int32_t* col_runs, void* q_bd, int32_t* err, void* stream);
 
 /*
  * Per-head V up-projection: replaces latent_ops.py:76-81 (`up_project`). a [T, 24, r_v] BF16 (strides a_st,
  * a_sh) x v_up_t [4, r_v, 256] BF16 (contiguous, U_v transposed) -> out [T, 24, 256] BF16 (strides out_st, out_sh),
- * written in place (e.g. a view of the first rows of the attention output).
+ * written in place (e.g. a view of the first rows of the attention output). err: as belt_block_diag_query.
  */
 int belt_up_project(const void* a, int64_t num_tokens, int64_t a_st, int64_t a_sh, int32_t r_v, const void* v_up_t,
-                    void* out, int64_t out_st, int64_t out_sh, void* stream);
+                    void* out, int64_t out_st, int64_t out_sh, int32_t* err, void* stream);
 
 /*
  * Latent cache write: replaces latent_ops.py:138-158 (`latent_rows_to_cache`, kernel `_latent_rows` :85-135).
@@ -141,8 +142,8 @@ int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, con
                         float* lse, int64_t lse_sb, void* stream);
 
 /*
- * One decode step of a compressed layer with no caller-provided scratch: belt_decode_schedule, belt_latent_decode
- * and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
+ * One decode step of a compressed layer with no caller-provided scratch: belt_decode_schedule_weighted (start cost
+ * 10, the backend's split), belt_latent_decode and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
  * 24 MiB array inside this library instead of buffers from the caller. It has no counterpart in the reference
  * (whose decode allocates its partials per call); it exists for callers that cannot allocate device memory: hosts
  * binding this ABI that hold only the engine's KV pool, query and output buffers, and engines that reserved nearly
@@ -151,10 +152,13 @@ int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, con
  *   merged outputs out [num_reqs, 24, lv] BF16 (strides out_sb, out_sh) and lse [num_reqs, 24] fp32 (row stride
  *   lse_sb), as belt_merge_segments. Pointers and `stream` belong to the current device.
  *   Limits (BELT_ERR_INVALID beyond them, before anything runs): num_reqs <= 4096, num_ctas <= 1024, and
- *   (num_reqs + num_ctas) * 24 * (lv + 1) * 4 bytes <= 24 MiB - 128 KiB (lv = 640, 148 CTAs: 259 requests).
- *   The first call on a device looks up the array's device address (cudaGetSymbolAddress) for that device; make it
- *   before any stream capture begins. All calls on a device share the array and leave their contents in it; calls
- *   that overlap on the GPU (unordered streams or host threads of one device) race on it.
+ *   (num_reqs + num_ctas) * 24 * (lv + 1) * 4 bytes <= 24 MiB - 128 KiB (lv = 640, 148 CTAs: 258 requests).
+ *   The array's device address belongs to the CUDA context: a call outside stream capture looks it up
+ *   (cudaGetSymbolAddress) and records it for the current context; a call during capture uses that record and is
+ *   refused if the context has none. Make the first call in a context (a device's first, the first under a
+ *   driver-API context, the first after cudaDeviceReset) before any stream capture begins. All calls on a device
+ *   share the array and leave their contents in it; calls that overlap on the GPU (unordered streams or host threads
+ *   of one device) race on it.
  */
 int belt_latent_decode_noalloc(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
                                int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,

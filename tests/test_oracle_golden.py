@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import oracle
-from belt_b200 import export_latent, synth
+from belt_b200 import latent_format, synth
 
 from conftest import CASES, bf16_ulp_close, golden_case, sha
 
@@ -29,7 +29,8 @@ def test_inputs_regenerate(case):
 
 
 def test_export_matches_reference(case):
-    """The product's and the oracle's ``build_latent_layer`` give the reference's tensors bit for bit."""
+    """The product's ``latent_tensors`` and the oracle's ``build_latent_layer`` give the reference's tensors bit for
+    bit."""
     name, fx, spec, w, batch, q, layer = case
     assert w.layout == fx["layout"]
     assert sha(w.kv_latent_proj) == fx["factors_sha"]["kv_latent_proj"]
@@ -41,9 +42,12 @@ def test_export_matches_reference(case):
         fx["factors_sha"]["kv_latent_proj"]
     for r_k, r_v in [(512, 512), (448, 576), (640, 384)]:
         ranks = [r_k // 4] * 4
-        assert export_latent.row_layout(ranks, r_v, 4, 64) == oracle.row_layout(ranks, r_v, 64)
-        assert export_latent.row_layout(ranks, r_v, 4, 64, rope_align=True) == \
+        assert latent_format.row_layout(ranks, r_v, 64) == oracle.row_layout(ranks, r_v, 64)
+        assert latent_format.row_layout(ranks, r_v, 64, rope_align=True) == \
             oracle.row_layout(ranks, r_v, 64, rope_align=True)
+    for ranks in ([96, 112, 144, 160], [48, 40, 64, 56], [64, 16, 64, 8]):
+        assert latent_format.row_layout(ranks, 300, 64, rope_align=True) == \
+            oracle.row_layout(ranks, 300, 64, rope_align=True)
 
 
 def test_derive_matches_reference(case):
