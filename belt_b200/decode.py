@@ -16,6 +16,7 @@ import math
 import torch
 
 from . import _lib
+from . import ops as _ops  # noqa: F401  (registers torch.ops.lrkv_b200)
 
 H, G, ROT = 24, 4, 64
 TILE_T = 128          # tokens per split-KV tile (BELT_DECODE_TILE)
@@ -99,15 +100,8 @@ def schedule(sched: DecodeSchedule, seq_lens: torch.Tensor, min_tiles: int = 1) 
         raise ValueError(f"schedule: {B} requests exceed the schedule's capacity {sched.seg_base.shape[0] - 1}")
     if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
         raise ValueError("schedule: seq_lens must be contiguous int32")
-    dev = seq_lens.device
-    if sched.start_cost > 0:
-        _lib.call("belt_decode_schedule_weighted", seq_lens.data_ptr(), B, sched.num_ctas, min_tiles,
-                  sched.start_cost, sched.work.data_ptr(), sched.work.shape[0], sched.cta_seg.data_ptr(),
-                  sched.seg_base.data_ptr(), error_word(dev).data_ptr(), _stream_ptr(dev))
-    else:
-        _lib.call("belt_decode_schedule", seq_lens.data_ptr(), B, sched.num_ctas, min_tiles, sched.work.data_ptr(),
-                  sched.work.shape[0], sched.cta_seg.data_ptr(), sched.seg_base.data_ptr(),
-                  error_word(dev).data_ptr(), _stream_ptr(dev))
+    torch.ops.lrkv_b200.decode_schedule(seq_lens, sched.work, sched.cta_seg, sched.seg_base, sched.num_ctas,
+                                        int(min_tiles), int(sched.start_cost))
 
 
 def block_diag_query(q_lat: torch.Tensor, q_rot: torch.Tensor, k_off: list, k_ranks: list, lk_pad: int,
@@ -152,7 +146,7 @@ def rope_blocks(u_rot: list, groups) -> torch.Tensor:
 def _check_cache(cache: torch.Tensor):
     if cache.dtype != torch.bfloat16 or cache.dim() != 3 or cache.stride(-1) != 1:
         raise ValueError("cache must be a [blocks, page, W] BF16 view with contiguous rows")
-    if cache.stride(1) % 8 or cache.stride(0) % 8 or cache.data_ptr() % 16:
+    if cache.stride(1) % 8 or cache.stride(0) % 8:
         raise ValueError("cache rows must start 16-byte aligned")
 
 
@@ -183,14 +177,9 @@ def latent_decode(q_bd: torch.Tensor, cache: torch.Tensor, block_table: torch.Te
         raise ValueError("rope blocks must be contiguous BF16 [1, 64, n * 64]")
     if cos_sin.dtype != torch.bfloat16 or not cos_sin.is_contiguous() or cos_sin.shape[1] != ROT:
         raise ValueError("cos_sin must be contiguous BF16 [max_pos, 64]")
-    groups = [x for gr in rope.groups for x in gr]
-    dev = q_bd.device
-    _lib.call("belt_latent_decode", q_bd.data_ptr(), B, q_bd.shape[2], cache.data_ptr(), cache.shape[0],
-              cache.shape[1], cache.shape[2], cache.stride(0), cache.stride(1), block_table.data_ptr(),
-              block_table.stride(0), seq_lens.data_ptr(), sched.work.data_ptr(), sched.cta_seg.data_ptr(),
-              sched.num_ctas, part.data_ptr(), part.stride(0), part.stride(1), float(sm_scale), int(lk_pad), int(lv),
-              _lib.int_array(groups), blocks.data_ptr(), blocks.shape[2] // CHUNK, cos_sin.data_ptr(),
-              cos_sin.shape[0], error_word(dev).data_ptr(), _stream_ptr(dev))
+    groups = [int(x) for gr in rope.groups for x in gr]
+    torch.ops.lrkv_b200.latent_decode(q_bd, cache, block_table, seq_lens, sched.work, sched.cta_seg, part,
+                                      sched.num_ctas, float(sm_scale), int(lk_pad), int(lv), groups, blocks, cos_sin)
 
 
 latent_decode_cute = latent_decode   # the reference's name for the same entry
@@ -204,6 +193,4 @@ def merge_segments(part: torch.Tensor, sched: DecodeSchedule, out: torch.Tensor,
         raise ValueError("merge_segments: out must be BF16 [B, H, lv] with a contiguous last dim")
     if lse.dtype != torch.float32 or lse.stride(-1) != 1:
         raise ValueError("merge_segments: lse must be fp32 [B, H]")
-    dev = out.device
-    _lib.call("belt_merge_segments", part.data_ptr(), part.stride(0), part.stride(1), sched.seg_base.data_ptr(), B,
-              nh, lv, out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), _stream_ptr(dev))
+    torch.ops.lrkv_b200.merge_segments(part, sched.seg_base, out, lse)

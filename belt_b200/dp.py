@@ -90,6 +90,15 @@ class HostGroup:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
         return float(t.item())
 
+    def gather_float(self, x: float) -> list:
+        """Every rank's ``x``, in rank order (a one-element list on a single rank)."""
+        if self.dist is None:
+            return [float(x)]
+        import torch
+        out = [torch.zeros(1, dtype=torch.float64) for _ in range(self.world)]
+        self.dist.all_gather(out, torch.tensor([float(x)], dtype=torch.float64))
+        return [float(t.item()) for t in out]
+
     def close(self) -> None:
         if self.dist is not None:
             self.dist.destroy_process_group()

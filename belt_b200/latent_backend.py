@@ -273,12 +273,11 @@ class LatentAttentionImpl:
         lat: LatentLayer = layer.latent
         cache = kv_cache[:, 0]                    # [blocks, block_size, row_width], strided per block
         nd = m.num_decode_tokens
-        main = torch.cuda.current_stream(query.device)
         if m.num_decodes:
             dev = query.device
             q_bd = lat.block_diag_query(query[:nd])
             if side is not None:
-                main.wait_stream(side)            # the step's own rows are part of the context
+                torch.cuda.current_stream(dev).wait_stream(side)   # the step's own rows are part of the context
                 side = None
             part = torch.empty(nd + m.sched.num_ctas, self.num_heads, lat.v_rank + 1, dtype=torch.float32,
                                device=dev)
@@ -289,7 +288,7 @@ class LatentAttentionImpl:
             dec.merge_segments(part, m.sched, a, lse)
             lat.up_project(a, output[:nd])
         if side is not None:
-            main.wait_stream(side)
+            torch.cuda.current_stream(query.device).wait_stream(side)
         if m.num_prefills:
             self._prefill(lat, query, output, cache, m)
         return output

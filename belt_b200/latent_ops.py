@@ -19,8 +19,7 @@ from __future__ import annotations
 
 import torch
 
-from . import _lib
-from .decode import _stream_ptr, error_word
+from . import ops as _ops  # noqa: F401  (registers torch.ops.lrkv_b200)
 
 HEAD_DIM = 256
 
@@ -59,12 +58,9 @@ def block_diag_query(q: torch.Tensor, qmap: torch.Tensor, col_runs=None) -> torc
         raise ValueError("block_diag_query: BF16 q with a contiguous last dim and a contiguous BF16 qmap")
     if Hq != 24 or D != HEAD_DIM or qmap.shape[0] != 4 or qmap.shape[1] != D:
         raise ValueError(f"block_diag_query: q {tuple(q.shape)} / qmap {tuple(qmap.shape)} (24 heads, 4 groups, 256)")
-    out = torch.empty(T, Hq, KQ, device=q.device, dtype=q.dtype)
     runs = col_runs if col_runs is not None else _runs_dense(KQ)
-    flat = [x for g in runs for r in g for x in r]
-    _lib.call("belt_block_diag_query", q.data_ptr(), T, q.stride(0), q.stride(1), qmap.data_ptr(), KQ,
-              _lib.int_array(flat), out.data_ptr(), error_word(q.device).data_ptr(), _stream_ptr(q.device))
-    return out
+    flat = [int(x) for g in runs for r in g for x in r]
+    return torch.ops.lrkv_b200.block_diag_query(q, qmap, flat)
 
 
 def up_project(a: torch.Tensor, v_up_t: torch.Tensor, out: torch.Tensor) -> None:
@@ -77,8 +73,7 @@ def up_project(a: torch.Tensor, v_up_t: torch.Tensor, out: torch.Tensor) -> None
         raise ValueError("up_project: shapes / strides")
     if a.dtype != torch.bfloat16 or out.dtype != torch.bfloat16 or v_up_t.dtype != torch.bfloat16:
         raise ValueError("up_project: BF16 tensors")
-    _lib.call("belt_up_project", a.data_ptr(), a.shape[0], a.stride(0), a.stride(1), R, v_up_t.data_ptr(),
-              out.data_ptr(), out.stride(0), out.stride(1), error_word(a.device).data_ptr(), _stream_ptr(a.device))
+    torch.ops.lrkv_b200.up_project(a, v_up_t, out)
 
 
 def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: torch.Tensor, u_cat: torch.Tensor,
@@ -105,10 +100,7 @@ def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: tor
         raise ValueError(f"latent_rows_to_cache: c has {c.shape[1]} columns, the row width is {W}")
     if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous():
         raise ValueError("latent_rows_to_cache: contiguous int32 / int64 slot_mapping")
-    _lib.call("belt_latent_rows_to_cache", c.data_ptr(), T, c.stride(0), slot_mapping.data_ptr(),
-              int(slot_mapping.dtype == torch.int64), cache.data_ptr(), cache.shape[0], cache.shape[1], W,
-              cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk, _lib.int_array(segs), float(eps),
-              _stream_ptr(c.device))
+    torch.ops.lrkv_b200.cache_write(c, slot_mapping, cache, u_cat, segs, float(eps))
 
 
 # From this many tokens on (prefill chunks) the projection runs as a library GEMM followed by the cache write: the fused
@@ -143,10 +135,7 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
     if not fused:
         latent_rows_to_cache(x[:T] @ w_down[:W].T, slot_mapping, cache, u_cat, k_segs, eps)
         return
-    _lib.call("belt_latent_proj_rows_to_cache", x.data_ptr(), T, x.stride(0), x.shape[1], w_down.data_ptr(),
-              w_down.stride(0), slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), cache.data_ptr(),
-              cache.shape[0], cache.shape[1], W, cache.stride(0), cache.stride(1), u_cat.data_ptr(), lk,
-              _lib.int_array(segs), float(eps), error_word(x.device).data_ptr(), _stream_ptr(x.device))
+    torch.ops.lrkv_b200.proj_cache_write(x, w_down, slot_mapping, cache, u_cat, segs, float(eps))
 
 
 def decompress_paged(cache: torch.Tensor, block_table_row: torch.Tensor, seq_len: int, pos0: int, count: int,
@@ -174,11 +163,8 @@ def decompress_paged(cache: torch.Tensor, block_table_row: torch.Tensor, seq_len
             raise ValueError(f"decompress_paged: {name} [count, 4, 256] BF16 with contiguous channels")
     if k_out.stride() != v_out.stride():
         raise ValueError("decompress_paged: k_out and v_out with the same strides")
-    _lib.call("belt_latent_decompress", cache.data_ptr(), cache.shape[0], cache.shape[1], cache.shape[2],
-              cache.stride(0), cache.stride(1), block_table_row.data_ptr(), int(seq_len), int(pos0), int(count),
-              wk.data_ptr(), kc, _lib.int_array(host_k_segs(k_segs)), v_up_t.data_ptr(), int(v_offset), r_v,
-              cos_sin.data_ptr(), cos_sin.shape[0], k_out.data_ptr(), v_out.data_ptr(), k_out.stride(0),
-              k_out.stride(1), error_word(dev).data_ptr(), _stream_ptr(dev))
+    torch.ops.lrkv_b200.decompress(cache, block_table_row, int(seq_len), int(pos0), wk, host_k_segs(k_segs), v_up_t,
+                                   int(v_offset), cos_sin, k_out, v_out)
     return k_out, v_out
 
 
@@ -204,8 +190,5 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos0:
         raise ValueError("prefill_attention: q [ql, 24, 256], k / v [S, 4, 256] with equal strides, out like q")
     if lse.dtype != torch.float32 or tuple(lse.shape) != (ql, H) or lse.stride(1) != 1:
         raise ValueError("prefill_attention: lse [ql, 24] fp32 with contiguous heads")
-    _lib.call("belt_prefill_attention", q.data_ptr(), ql, q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), S,
-              k.stride(0), k.stride(1), int(q_pos0), int(k_pos0), int(bool(causal)), float(scale), out.data_ptr(),
-              out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0), error_word(dev).data_ptr(),
-              _stream_ptr(dev))
+    torch.ops.lrkv_b200.prefill_attention(q, k, v, int(q_pos0), int(k_pos0), float(scale), bool(causal), out, lse)
     return out, lse

@@ -1,11 +1,13 @@
 """Benchmark of the latent-KV decode step on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3|2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 3|1|2|4|5] [--impl ours|reference]
 
-Workload (the headline configuration the north star names, per GPU): 16 compressed full-attention layers with learned
-per-layer ranks (r_k from {384, 448, 512, 576, 640}, r_v = 1024 - r_k, row width 1024), batch 128, context lengths
-log-uniform in [1k, 64k], block size 16, BF16, random-permuted block tables, one block holding all 16 layers' pages
-(block-outermost, strided per-layer views). ``--config 2`` runs the single-layer c50 case (batch 64 x 8192).
+Workload (the headline configuration, per GPU): 16 compressed full-attention layers with learned per-layer ranks (r_k
+from {384, 448, 512, 576, 640}, r_v = 1024 - r_k, row width 1024), batch 128, context lengths log-uniform in
+[1k, 64k], block size 16, BF16, random-permuted block tables, one block holding all 16 layers' pages
+(block-outermost, strided per-layer views). ``--config 2`` runs the single-layer c50 case (batch 64 x 8192),
+``--config 4`` the long-context case (batch 32 x 65,536, ``--rows c25`` for the narrow rows), ``--config 1`` the
+CPU-runnable case (4 requests, one layer; for the reference arm).
 
 A step is one decode step of the path over the batch: the split-KV schedule once, then per layer the cache write of
 the new token's row, the absorbed block-diagonal query, the decode kernel, the segment merge and the U_v
@@ -14,8 +16,21 @@ max over ranks); the cache (tens of GB) is far larger than L2, so every step str
 step through the backend's public API (``LatentAttentionImpl.forward``) from pinned host buffers: this step's queries
 and latent rows are copied in and the attention outputs copied out inside the timed region.
 
-Multi-GPU: one process per GPU (torchrun), each with its own 128 sequences (weak scaling, data parallel, no
-collective on the data path; a gloo barrier and a max over ranks only bracket the timing).
+After the timed steps the CPU leg runs the CPU restatement of the reference's path (``oracle``): as the checker of a
+sample of the step just timed (``parity``: the outputs of 4 requests spanning the length range in 3 layers of
+different ranks, against the fp32 oracle at max-abs 2e-2 / mean-abs 2e-3), and, at N = 1, timed on a bounded sample
+as ``cpu_baseline``.
+
+Multi-GPU: one process per GPU (torchrun), each with its own 128 sequences of the same lengths as the one-GPU run
+(weak scaling with fixed work per GPU, data parallel, no collective on the data path; a gloo barrier and a max over
+ranks only bracket the timing).
+
+``--config 5`` is the box-level serving run: 1,024 sequences (config-3 ranks and lengths) partitioned across the N
+ranks by LPT, each rank serving its share in waves that fit its HBM (two wave buffers: one decoding, the next one
+being prefilled); every wave is prefilled by chunked latent cache writes of 8,192 tokens per layer (down-projection
++ paged scatter), then decoded for 256 steps with this step's cache write, the next wave's prefill chunks interleaved
+between the decode steps. ``value`` = 1,024 x 256 decode tokens / max rank time (strong scaling: the total work is
+fixed).
 """
 
 from __future__ import annotations
@@ -48,7 +63,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", type=int, default=3, choices=[2, 3, 4])
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--rows", default="c50", choices=["c50", "c25"],
                     help="config 4 row format: c50 (r_k = r_v = 512, 1024-column rows) or c25 (256 + 256, 512 columns)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -56,6 +71,12 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of one baseline sample")
+    ap.add_argument("--cpu-full", action="store_true",
+                    help="reference arm: time the whole workload (every request of every layer), no extrapolation")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed step's outputs")
+    ap.add_argument("--decode-steps", type=int, default=256, help="config 5: decode steps per wave")
+    ap.add_argument("--prefill-chunk", type=int, default=8192, help="config 5: tokens per chunked-prefill write")
+    ap.add_argument("--num-seqs", type=int, default=1024, help="config 5: sequences on the box")
     ap.add_argument("--prefill", action="store_true",
                     help="measure the prefill path instead (one GPU): keys / values rebuilt from the paged rows and "
                          "causal attention of 8192 new tokens over an 8192-token context, one c50 layer")
@@ -64,26 +85,45 @@ def parse_args():
 
 # ------------------------------------------------------------------------------------------------------------ workload
 def workload_spec(config: int, batch: int | None, rank: int, world: int, rows: str = "c50"):
-    """(layer specs, this rank's seq_lens, page, description, partition imbalance). The box holds batch x world
-    requests; ranks take LPT shares by context tokens (equal counts), so every rank decodes ~batch requests."""
+    """(layer specs, this rank's seq_lens, page, description). Config 3 gives every rank the same request lengths
+    (the one-GPU pool of ``batch`` requests), so the work per GPU is the same at every N."""
+    if config == 1:
+        return [synth.c50()], [129, 513, 1025, 2001], 16, {
+            "workload": "config1: 1 layer c50, 4 requests with contexts {128, 512, 1024, 2000} + this step's, page 16"}
     if config == 2:
         B = batch or 64
-        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}, 1.0
+        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}
     if config == 4:
         # long context: every request 65,536 cached tokens + this step's, 512 tiles each over the CTAs
         B = batch or 32
         spec = synth.c25() if rows == "c25" else synth.c50()
         return [spec] * 16, [65536 + 1] * B, 16, {
-            "workload": f"config4: 16 layers {rows} (rows of {spec.row_width} columns), batch 32 x 65536, page 16"}, 1.0
-    B = batch or 128
+            "workload": f"config4: 16 layers {rows} (rows of {spec.row_width} columns), batch 32 x 65536, page 16"}
     ranks = synth.learned_ranks(16)
-    pool = synth.log_uniform_lengths(B * world, 1024, 65536, seed=synth.SEED_LENGTHS)
-    parts = dp.partition_lpt(pool, world)
-    lens = [pool[i] for i in parts[rank]]
     specs = [synth.spec_from_ranks(rk, rv) for rk, rv in ranks]
+    if config == 5:
+        n = batch or 1024
+        return specs, serving_pool(n), 16, {
+            "workload": f"config5: {n} sequences on the box, 16 layers with config-3 ranks, context log-uniform "
+                        "[1k, 64k], page 16"}
+    B = batch or 128
+    lens = synth.log_uniform_lengths(B, 1024, 65536, seed=synth.SEED_LENGTHS)
     return specs, [L + 1 for L in lens], 16, {
         "workload": "config3: 16 layers, learned ranks (r_k in {384..640}, r_v = 1024 - r_k), batch 128/GPU, "
-                    "context log-uniform [1k, 64k], page 16"}, dp.imbalance(pool, parts)
+                    "context log-uniform [1k, 64k], page 16"}
+
+
+def serving_pool(n: int) -> list:
+    """Prompt lengths of config 5's ``n`` sequences (the config-3 distribution, seeded apart from config 3's pool)."""
+    return synth.log_uniform_lengths(n, 1024, 65536, seed=synth.SEED_LENGTHS + 50)
+
+
+def load_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
 
 
 class Workload:
@@ -279,69 +319,161 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples), "power_w_max": max(power), "source": self.source}
 
 
-# ------------------------------------------------------------------------------------------------------------ CPU arm
-def cpu_reference_rate(specs, seq_lens, page, budget_s: float, rank: int = 0):
-    """Decode tokens/s of the reference's torch path (the oracle port of ``LatentLayer.decompress`` + fp32 attention)
-    on this host's cores, extrapolated to the whole workload from a bounded sample of requests of the first layer.
-    Returns (tokens/s, cores, sample description, seconds)."""
-    import oracle
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    w = synth.make_layer(specs[0], seed=synth.SEED_FACTORS)
-    total_ctx = sum(seq_lens)
-    # calibrate on a short request, then size the sample to the budget
-    order = sorted(range(len(seq_lens)), key=lambda i: seq_lens[i])
-    probe = [seq_lens[order[len(order) // 2]]]
-    t_probe = _cpu_time(w, probe, page)
-    per_tok = t_probe / sum(probe)
-    want = max(1, int(budget_s / per_tok))
-    sample, acc = [], 0
-    for i in order[len(order) // 4:] + order[:len(order) // 4]:
-        if acc + seq_lens[i] > want and sample:
-            break
-        sample.append(seq_lens[i])
-        acc += seq_lens[i]
-    t = _cpu_time(w, sample, page)
-    per_tok = t / sum(sample)
-    step_s = per_tok * total_ctx * len(specs)                 # every layer of every sequence
-    rate = len(seq_lens) / step_s
-    desc = (f"oracle port of the reference torch path (decompress + fp32 attention), layer 0, {len(sample)} requests "
-            f"/ {sum(sample)} context tokens timed ({t:.1f} s), extrapolated per context token to {len(specs)} layers "
-            f"x {total_ctx} tokens")
-    return rate, cores, desc, t
+# ------------------------------------------------------------------------------------------------------------ CPU leg
+# The CPU restatement of the reference's path (``oracle``) runs only here: as the checker of the outputs of the step the
+# GPU just timed (``parity``) and as the CPU baseline / reference arm (timed on a bounded sample). Nothing in a timed
+# GPU region touches it.
+PARITY_MAX_ABS, PARITY_MEAN_ABS = 2e-2, 2e-3       # the north-star tolerance for BF16 attention outputs
 
 
-def _cpu_time(w, lens, page):
+def parity_picks(lens, r_k, n_reqs: int = 4):
+    """(layers, requests) checked after the timed region: the layers whose K rank is nearest to 384, 512 and 640 (one
+    per distinct rank), and ``n_reqs`` requests at even steps through the length order (shortest to longest)."""
+    layers = []
+    for target in (384, 512, 640):
+        best = min(range(len(r_k)), key=lambda l: (abs(r_k[l] - target), l))
+        if best not in layers:
+            layers.append(best)
+    order = sorted(range(len(lens)), key=lambda b: (lens[b], b))
+    n = min(n_reqs, len(order))
+    reqs = sorted({order[round(i * (len(order) - 1) / max(1, n - 1))] for i in range(n)})
+    return layers, reqs
+
+
+def gather_parity(buf, block_table, lens, page, q, out, layers, reqs):
+    """Host copies, made after the timed region, of what the check needs: per (layer, request) the GPU output, the
+    query and the request's cache pages of that layer (``buf`` [blocks, layers, page, W])."""
+    bt = block_table.cpu()
+    items = []
+    for l in layers:
+        for b in reqs:
+            n = int(lens[b])
+            blocks = bt[b, :-(-n // page)].long()
+            items.append({"layer": l, "req": b, "seq_len": n, "out": out[l][b].float().cpu(), "q": q[l][b].cpu(),
+                          "pages": buf[blocks.to(buf.device), l].cpu()})
+    return items
+
+
+def check_parity(weights, items) -> dict:
+    """The gathered GPU outputs against the fp32 oracle (``oracle.decode_fp32``) on the same cache rows."""
     import oracle
-    cos_sin = synth.cos_sin_table(max(lens) + 1)
-    ref = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin)
-    batch = synth.make_batch(w.layout, lens, page=page, seed=synth.SEED_CACHE, poison=False)
-    q = synth.make_queries(len(lens))
+    cos_sin = synth.cos_sin_table(max(it["seq_len"] for it in items) + 1)
+    refs = {}
+    worst, total, count = 0.0, 0.0, 0
     t0 = time.perf_counter()
-    oracle.decode_reference(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
-    return time.perf_counter() - t0
+    for it in items:
+        l = it["layer"]
+        if l not in refs:
+            w = weights[l]
+            refs[l] = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin)
+        pages = it["pages"]
+        bt = torch.arange(pages.shape[0], dtype=torch.int32)[None]
+        exp = oracle.decode_fp32(it["q"][None], pages, bt, torch.tensor([it["seq_len"]]), refs[l], SCALE)[0]
+        d = (it["out"] - exp).abs()
+        worst = max(worst, float(d.max()))
+        total += float(d.sum())
+        count += d.numel()
+    mean = total / max(1, count)
+    return {"max_abs": worst, "mean_abs": mean, "ok": bool(worst < PARITY_MAX_ABS and mean < PARITY_MEAN_ABS),
+            "tolerance": {"max_abs": PARITY_MAX_ABS, "mean_abs": PARITY_MEAN_ABS}, "oracle": "decode_fp32",
+            "layers": sorted({it["layer"] for it in items}), "requests": sorted({it["req"] for it in items}),
+            "context_tokens": sorted({it["seq_len"] for it in items}), "cpu_seconds": time.perf_counter() - t0}
+
+
+class CpuArm:
+    """The reference's torch path restated on the CPU (``oracle.decode_reference``: ``LatentLayer.decompress`` of every
+    context row, then fp32 attention) on all host cores. A bounded sample of layer 0's requests is timed and the time
+    per context token extrapolated to the workload (every layer of every request), unless ``full``: then every
+    request of every layer is timed and nothing is extrapolated."""
+
+    def __init__(self, specs, seq_lens, page, budget_s: float, full: bool = False):
+        import oracle
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
+        self.specs, self.seq_lens, self.page, self.full = specs, list(seq_lens), page, full
+        self.layers = list(range(len(specs))) if full else [0]
+        self.total_ctx = sum(self.seq_lens)
+        if full:
+            self.sample = list(self.seq_lens)
+        else:
+            # calibrate on the median request, then take requests from the 25th percentile up to the budget
+            order = sorted(range(len(self.seq_lens)), key=lambda i: self.seq_lens[i])
+            probe = [self.seq_lens[order[len(order) // 2]]]
+            per_tok = self._time_layer(0, probe) / sum(probe)
+            want = max(1, int(budget_s / per_tok))
+            self.sample, acc = [], 0
+            for i in order[len(order) // 4:] + order[:len(order) // 4]:
+                if acc + self.seq_lens[i] > want and self.sample:
+                    break
+                self.sample.append(self.seq_lens[i])
+                acc += self.seq_lens[i]
+        self._prepared = {l: self._prepare(l, self.sample) for l in self.layers}
+        self._oracle = oracle
+
+    def _prepare(self, l, lens):
+        import oracle
+        w = synth.make_layer(self.specs[l], seed=synth.SEED_FACTORS + l)
+        ref = oracle.derive(w.k_up, w.v_up, w.k_norm_weight, w.layout, synth.cos_sin_table(max(lens) + 1))
+        batch = synth.make_batch(w.layout, lens, page=self.page, seed=synth.SEED_CACHE + 101 * l, poison=False)
+        return ref, batch, synth.make_queries(len(lens))
+
+    def _time_layer(self, l, lens, prepared=None):
+        import oracle
+        ref, batch, q = prepared or self._prepare(l, lens)
+        t0 = time.perf_counter()
+        oracle.decode_reference(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+        return time.perf_counter() - t0
+
+    def run_once(self) -> float:
+        """Seconds for one pass over the sample (every sampled layer)."""
+        return sum(self._time_layer(l, self.sample, self._prepared[l]) for l in self.layers)
+
+    def rate(self, seconds: float) -> float:
+        """Decode tokens/s of the whole workload implied by one pass that took ``seconds``."""
+        if self.full:
+            return len(self.seq_lens) / seconds
+        per_tok = seconds / sum(self.sample)
+        return len(self.seq_lens) / (per_tok * self.total_ctx * len(self.specs))
+
+    def describe(self, seconds: float) -> str:
+        if self.full:
+            return (f"oracle port of the reference torch path (decompress + fp32 attention): the whole workload timed, "
+                    f"{len(self.layers)} layers x {len(self.sample)} requests / {sum(self.sample)} context tokens "
+                    f"({seconds:.1f} s), not extrapolated")
+        return (f"oracle port of the reference torch path (decompress + fp32 attention), layer 0, {len(self.sample)} "
+                f"requests / {sum(self.sample)} context tokens timed ({seconds:.1f} s), extrapolated per context token "
+                f"to {len(self.specs)} layers x {self.total_ctx} tokens")
 
 
 def run_reference_arm(args, rank, world):
-    """The reference's CPU path on the whole box's requests (every rank's share), rank 0 only."""
+    """The reference's CPU path on the box's requests (every rank's share), rank 0 only."""
     if rank != 0:
         return
-    per_gpu = args.batch or {2: 64, 3: 128, 4: 32}[args.config]
-    specs, seq_lens, page, cfg, _ = workload_spec(args.config, per_gpu * world, 0, 1, args.rows)
-    rates, tsum = [], 0.0
-    for i in range(args.warmup + args.steps):
-        budget = min(args.cpu_seconds, 240.0 / max(1, args.warmup + args.steps))
-        rate, cores, desc, t = cpu_reference_rate(specs, seq_lens, page, budget)
+    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, 0, 1, args.rows)
+    seq_lens = list(seq_lens) * (world if args.config == 3 else 1)      # every rank holds the same lengths
+    n = args.warmup + args.steps
+    budget = min(args.cpu_seconds, 150.0 / max(1, n))
+    arm = CpuArm(specs, seq_lens, page, budget, full=args.cpu_full)
+    rates, secs = [], []
+    for i in range(n):
+        t = arm.run_once()
         if i >= args.warmup:
-            rates.append(rate)
-            tsum += t
+            rates.append(arm.rate(t))
+            secs.append(t)
     value = statistics.median(rates)
     ms = 1000.0 * len(seq_lens) / value
+    timed_tokens = sum(arm.sample) * len(arm.layers)
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if args.config == 3 else "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference", "extrapolated": not arm.full,
+            "samples": {"timed_passes": len(secs), "seconds_per_pass": statistics.median(secs),
+                        "timed_context_tokens_per_pass": timed_tokens, "timed_layers": len(arm.layers),
+                        "timed_requests": len(arm.sample), "workload_layers": len(specs),
+                        "workload_context_tokens": sum(seq_lens)},
             "config": {**cfg, "global_batch": len(seq_lens), "parallelism": "dp (rank 0 only: CPU)"},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": arm.cores, "kind": "port",
+                             "sample": arm.describe(statistics.median(secs))},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -507,6 +639,230 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------------ config 5
+def plan_waves(lens, steps: int, page: int, block_bytes: int, free_bytes: int):
+    """(waves, blocks per wave buffer, buffers): requests longest first, each wave as many as fit one buffer. One
+    buffer when everything fits at once, else two (one wave decoding while the next is prefilled)."""
+    need = [-(-(n + steps) // page) for n in lens]
+    if sum(need) * block_bytes <= free_bytes:
+        nbuf, cap = 1, sum(need)
+    else:
+        nbuf, cap = 2, free_bytes // 2 // block_bytes
+    waves, cur, used = [], [], 0
+    for i in sorted(range(len(lens)), key=lambda i: (-lens[i], i)):
+        if need[i] > cap:
+            raise RuntimeError(f"a sequence of {lens[i]} tokens does not fit a wave buffer of {cap} blocks")
+        if used + need[i] > cap:
+            waves.append(cur)
+            cur, used = [], 0
+        cur.append(i)
+        used += need[i]
+    if cur:
+        waves.append(cur)
+    return waves, cap, nbuf
+
+
+def wave_tables(base, npages, cap: int, steps: int, page: int, seed: int) -> dict:
+    """Host tables of one wave: a block table dealing ``npages[j]`` blocks of a seeded permutation of the buffer's
+    ``cap`` to request j; per decode step s the context lengths (base + s + 1) and the slot of that step's token
+    (position base + s); and the slots of every prompt position in request order (the prefill's token stream)."""
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(cap, generator=g)
+    base = torch.tensor(list(base), dtype=torch.int64)
+    bt = torch.zeros(len(base), max(npages), dtype=torch.int64)
+    off = 0
+    for j, n in enumerate(npages):
+        bt[j, :n] = perm[off:off + n]
+        off += n
+    pos = base[None, :] + torch.arange(steps)[:, None]                        # [steps, B]: this step's token
+    rows = torch.arange(len(base))[None, :].expand(steps, -1)
+    toks = torch.cat([torch.arange(int(n)) for n in base])
+    owner = torch.repeat_interleave(torch.arange(len(base)), base)
+    return {"block_table": bt, "seq_lens": (pos + 1).to(torch.int32), "slots": bt[rows, pos // page] * page + pos % page,
+            "prefill_slots": bt[owner, toks // page] * page + toks % page, "prefill_tokens": int(base.sum())}
+
+
+class ServingRun:
+    """Config 5 on one rank: its share of the box's sequences, served in waves that fit its HBM.
+
+    Every wave's cache lives in one of (at most) two wave buffers [blocks, layers, page, W]. A wave is first prefilled:
+    its prompts' latent rows are written by chunked cache writes of ``chunk`` tokens per layer (the down-projection of
+    the tokens' layer inputs + the paged scatter, ``latent_ops.project_rows_to_cache``), the chunks cut from the
+    wave's tokens in request order (a chunk can span requests, as a serving engine packs them). Then it is decoded for
+    ``steps`` steps: each step the schedule, and per layer the cache write of this step's token, the absorbed query,
+    the decode kernel, the merge and the U_v projection, with every request one token longer than the step before.
+    While wave k decodes, wave k + 1's prefill chunks run between its decode steps, into the other buffer."""
+
+    def __init__(self, specs, lens, page, device, rank, steps, chunk, reserve_bytes=10 << 30):
+        from belt_b200.layer import derive_latent_tensors
+        self.device, self.page, self.steps, self.chunk = device, page, steps, chunk
+        self.L = len(specs)
+        self.lens = list(lens)
+        cos_sin = synth.cos_sin_table(max(lens) + steps + 1)
+        self.weights = [synth.make_layer(sp, seed=synth.SEED_FACTORS + i) for i, sp in enumerate(specs)]
+        self.layers = [derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, cos_sin, device=device)
+                       for w in self.weights]
+        self.W = self.weights[0].layout["row_width"]
+        self.hidden = specs[0].hidden
+        self.w_down = [w.kv_latent_proj.to(device) for w in self.weights]
+        block_bytes = self.L * page * self.W * 2
+        free = torch.cuda.mem_get_info(device)[0] - reserve_bytes
+        self.waves, cap, nbuf = plan_waves(lens, steps, page, block_bytes, free)
+        need = [-(-(n + steps) // page) for n in lens]
+        self.cap, self.nbuf = cap, nbuf
+        Bmax = max(len(w) for w in self.waves)
+        gq = torch.Generator(device=device).manual_seed(synth.SEED_QUERY + 7 * rank)
+        # inputs of one decode step and of the prefill chunks: the work is what is timed, so a few buffers are reused
+        self.q = torch.randn(self.L, Bmax, H, D, generator=gq, device=device, dtype=torch.bfloat16)
+        self.x = torch.randn(self.L, Bmax, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
+        self.xp = torch.randn(4, chunk, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
+        self.sched = dec.make_schedule(Bmax, device)
+        self.part = torch.empty(Bmax + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
+        self.a = torch.empty(Bmax, H, 640, dtype=torch.bfloat16, device=device)
+        self.lse = torch.empty(Bmax, H, dtype=torch.float32, device=device)
+        self.out = torch.empty(self.L, Bmax, H, D, dtype=torch.bfloat16, device=device)
+        self.side = torch.cuda.Stream(device)
+        self.meta = [self._wave_meta(k, w, need, rank) for k, w in enumerate(self.waves)]
+        self.bufs = [torch.zeros(cap, self.L, page, self.W, dtype=torch.bfloat16, device=device)
+                     for _ in range(nbuf)]
+
+    def _wave_meta(self, k, reqs, need, rank):
+        """Block table, per-step seq_lens and slots, and the prefill slots of wave k, on the device."""
+        m = wave_tables([self.lens[i] for i in reqs], [need[i] for i in reqs], self.cap, self.steps, self.page,
+                        seed=synth.SEED_CACHE + 1000 * rank + k)
+        dev = self.device
+        return {"B": len(reqs), "block_table": m["block_table"].to(torch.int32).to(dev),
+                "seq_lens": m["seq_lens"].to(dev).contiguous(), "slots": m["slots"].to(dev).contiguous(),
+                "prefill_slots": m["prefill_slots"].to(dev), "prefill_tokens": m["prefill_tokens"],
+                "chunks": -(-m["prefill_tokens"] // self.chunk)}
+
+    def buffer(self, k):
+        return self.bufs[k % self.nbuf]
+
+    def decode_step(self, k, s):
+        m = self.meta[k]
+        B = m["B"]
+        buf = self.buffer(k)
+        seq_lens, slots = m["seq_lens"][s], m["slots"][s]
+        dec.schedule(self.sched, seq_lens)
+        main = torch.cuda.current_stream(self.device)
+        for l, lat in enumerate(self.layers):
+            cache = buf[:, l]
+            self.side.wait_stream(main)
+            with torch.cuda.stream(self.side):
+                latent_ops.project_rows_to_cache(self.x[l, :B], self.w_down[l], slots, cache, lat.u_cat,
+                                                 lat.k_segs_host, lat.eps)
+            q_bd = lat.block_diag_query(self.q[l, :B])
+            main.wait_stream(self.side)
+            part = self.part[:B + self.sched.num_ctas, :, :lat.v_rank + 1]
+            dec.latent_decode(q_bd, cache, m["block_table"], seq_lens, self.sched, part, SCALE, lat.v_offset,
+                              lat.v_rank, rope=lat.rope)
+            a = self.a[:B, :, :lat.v_rank]
+            dec.merge_segments(part, self.sched, a, self.lse[:B])
+            lat.up_project(a, self.out[l, :B])
+
+    def prefill_chunk(self, k, c):
+        m = self.meta[k]
+        t0 = c * self.chunk
+        n = min(self.chunk, m["prefill_tokens"] - t0)
+        slots = m["prefill_slots"][t0:t0 + n]
+        x = self.xp[c % self.xp.shape[0], :n]
+        buf = self.buffer(k)
+        for l, lat in enumerate(self.layers):
+            latent_ops.project_rows_to_cache(x, self.w_down[l], slots, buf[:, l], lat.u_cat, lat.k_segs_host, lat.eps)
+
+    def run(self, events=None):
+        """The whole serving run: wave 0's prefill, then every wave's decode steps with the next wave's prefill
+        chunks in between. ``events`` (start, end) pairs bracket the decode and the prefill work for the split."""
+        for c in range(self.meta[0]["chunks"]):
+            self.prefill_chunk(0, c)
+        for k in range(len(self.waves)):
+            nxt = k + 1 if k + 1 < len(self.waves) else None
+            n_next = self.meta[nxt]["chunks"] if nxt is not None else 0
+            per_step = -(-n_next // self.steps)
+            c = 0
+            for s in range(self.steps):
+                self.decode_step(k, s)
+                for _ in range(per_step):
+                    if c < n_next:
+                        self.prefill_chunk(nxt, c)
+                        c += 1
+
+    def launches(self) -> int:
+        """This repository's kernel launches in ``run`` (the prefill chunks' projection GEMM is a library call and is
+        counted apart, in ``library_gemm_launches``)."""
+        dec_steps = len(self.waves) * self.steps
+        return dec_steps * (1 + 5 * self.L) + sum(m["chunks"] for m in self.meta) * self.L
+
+
+def run_serving(args, group, dev):
+    rank, world = group.rank, group.world
+    specs, pool, page, cfg = workload_spec(5, args.num_seqs, rank, world)
+    parts = dp.partition_lpt(pool, world)
+    mine = [pool[i] for i in parts[rank]]
+    run = ServingRun(specs, mine, page, dev, rank, args.decode_steps, args.prefill_chunk)
+    # warm-up: a few decode steps of wave 0 and one prefill chunk (the timed run starts over from an empty cache)
+    for s in range(max(args.warmup, 3)):
+        run.decode_step(0, s)
+    run.prefill_chunk(0, 0)
+    torch.cuda.synchronize()
+    dec.check_device_errors(dev)
+    clocks = ClockSampler(dev)
+    group.barrier()
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    group.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    run.run()
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    group.barrier()
+    dec.check_device_errors(dev)
+    ms_local = start.elapsed_time(end)
+    ms = group.max(ms_local)
+    decode_tokens = len(pool) * args.decode_steps
+    value = decode_tokens / (ms / 1000.0)
+    per_rank_ms = group.gather_float(ms_local)
+    ctx = sum(mine)
+    # algorithmic HBM bytes of this rank's run: every decode step reads each request's context rows once per layer;
+    # every prefill chunk writes its rows (the down-projection's operands are counted in neither)
+    steps = args.decode_steps
+    dec_bytes = sum(sum(run.lens[i] + s + 1 for i in w for s in range(steps)) for w in run.waves) * run.L * run.W * 2
+    pf_bytes = ctx * run.L * run.W * 2
+    parity = None
+    if rank == 0 and not args.no_parity:
+        k = len(run.waves) - 1
+        m = run.meta[k]
+        lens_last = [run.lens[i] + steps for i in run.waves[k]]      # the last step's contexts
+        layers, reqs = parity_picks(lens_last, [w.layout["lk"] for w in run.weights], n_reqs=2)
+        items = gather_parity(run.buffer(k), m["block_table"], lens_last, page, run.q, run.out, layers[:2], reqs)
+        parity = check_parity(run.weights, items)
+    peaks = load_peaks()
+    peak_gbs = peaks.get("hbm_gbs") or 6650.0
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms / (len(run.waves) * steps), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {**cfg, "parallelism": f"dp{world}", "global_batch": len(pool),
+                       "partition": "LPT by context tokens, equal request counts",
+                       "partition_imbalance": dp.imbalance(pool, parts), "decode_steps_per_wave": steps,
+                       "prefill_chunk_tokens": args.prefill_chunk, "waves_rank0": len(run.waves),
+                       "wave_buffers_rank0": run.nbuf, "wave_buffer_gb_rank0": run.cap * run.L * page * run.W * 2 / 1e9,
+                       "context_tokens_rank0": ctx, "tokens_per_s_per_gpu": value / world,
+                       "ms_per_rank": per_rank_ms, "timed_ms": ms,
+                       "hbm_gb_per_s_rank0": (dec_bytes + pf_bytes) / (ms_local / 1000.0) / 1e9,
+                       "hbm_frac_rank0": (dec_bytes + pf_bytes) / (ms_local / 1000.0) / 1e9 / peak_gbs,
+                       "l2": "inputs larger than L2 (wave buffers of tens of GB)"},
+            "roofline": None, "clocks": clk, "gpu_launches": run.launches(),
+            "library_gemm_launches": sum(m["chunks"] for m in run.meta) * run.L}
+    if parity is not None:
+        line["parity"] = parity
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -524,7 +880,11 @@ def main():
     dev = torch.device("cuda", local)
     from belt_b200 import build as _build
     _build.build()
-    specs, seq_lens, page, cfg, imb = workload_spec(args.config, args.batch, rank, world, args.rows)
+    if args.config == 5:
+        run_serving(args, group, dev)
+        group.close()
+        return
+    specs, seq_lens, page, cfg = workload_spec(args.config, args.batch, rank, world, args.rows)
     wl = Workload(specs, seq_lens, page, dev, rank)
     torch.cuda.synchronize()
 
@@ -554,20 +914,21 @@ def main():
     dec.check_device_errors(dev)
     total_reqs = group.sum(wl.B)
     value = total_reqs / (ms / 1000.0)
+    # the outputs of the last timed step, for the oracle check (before anything else writes the cache)
+    parity_items = None
+    if rank == 0 and not args.no_parity:
+        layers, reqs = parity_picks(wl.seq_lens_list, [w.layout["lk"] for w in wl.weights])
+        parity_items = gather_parity(wl.buf, wl.block_table, wl.seq_lens_list, wl.page, wl.q, wl.out, layers, reqs)
 
     # the decode kernel's launches, per layer
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except (OSError, ValueError):
-        pass
+    peaks = load_peaks()
     peak_gbs = peaks.get("hbm_gbs") or 6650.0
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     kern_ms = [statistics.mean(dec_events[k][l][0].elapsed_time(dec_events[k][l][1]) for k in range(args.steps))
                for l in range(wl.L)]
     kern_bytes = [wl.decode_kernel_bytes(l) for l in range(wl.L)]
     achieved = sum(kern_bytes) / (sum(kern_ms) / 1000.0) / 1e9
+    rank_gbs = [group.gather_float(achieved)] if world > 1 else None
     step_gb = wl.step_bytes() / 1e9
     step_frac = step_gb / (ms_local / 1000.0) / peak_gbs
     traffic = read_traffic()
@@ -580,7 +941,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {**cfg, "global_batch": int(total_reqs), "per_gpu_batch": wl.B, "layers": wl.L,
                        "context_tokens_per_gpu": sum(wl.seq_lens_list), "parallelism": f"dp{world}",
-                       "partition": "LPT by context tokens, equal request counts", "partition_imbalance": imb,
+                       "partition": "every rank decodes the same request lengths (its own cache contents)",
                        "l2": "inputs larger than L2 (cache %.1f GB per GPU)" % (wl.buf.numel() * 2 / 1e9),
                        "tokens_per_s_per_gpu": value / world,
                        "step_roofline_frac": step_frac, "step_algorithmic_gb": step_gb},
@@ -590,18 +951,23 @@ def main():
                          "traffic": traffic_per_launch, "traffic_source": traffic and traffic.get("source")},
             "clocks": clk,
             "gpu_launches": wl.launches_per_step * args.steps}
+    if rank_gbs is not None:
+        line["roofline"]["achieved_per_rank"] = rank_gbs[0]
     if not args.no_e2e:
         _, e_ms_local, h2d, d2h = e2e_rate(wl, max(2, args.steps // 2), 2)
         e_ms = group.max(e_ms_local)
         line["e2e"] = {"value": total_reqs / (e_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                        "d2h_bytes_per_step": d2h, "ms_per_step": e_ms}
+    if parity_items is not None:
+        line["parity"] = check_parity(wl.weights, parity_items)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, cores, desc, t = cpu_reference_rate(specs, seq_lens, page, args.cpu_seconds)
-        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
+        arm = CpuArm(specs, seq_lens, page, args.cpu_seconds)
+        t = arm.run_once()
+        line["cpu_baseline"] = {"value": arm.rate(t), "unit": "tokens/s", "cores": arm.cores, "kind": "port",
+                                "sample": arm.describe(t)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     group.close()
-
 
 if __name__ == "__main__":
     main()
