@@ -16,7 +16,10 @@ more, joined before the decode reads the cache), then:
   kernel (``LatentLayer.decompress_paged``), causal attention on the tensor cores (``latent_ops.prefill_attention``),
   chunked with a log-sum-exp merge beyond ``PREFILL_CHUNK`` context tokens.
 
-The classes do not depend on vLLM: ``register_with_vllm`` installs them into a vLLM that provides the plugin API.
+When the running vLLM provides the plugin API the reference targets (``vllm_plugin.vllm_api``), the backend, the KV
+spec and the attention-type / block-size types are vLLM's own classes (``LatentAttentionBackend`` subclasses vLLM's
+``AttentionBackend``, ``LatentKVSpec`` its ``FullAttentionSpec``); without it, stand-ins of the same shape are used and
+the package runs on its own. ``vllm_plugin.register`` installs the backend into vLLM.
 """
 
 from __future__ import annotations
@@ -28,7 +31,7 @@ from typing import ClassVar
 import torch
 
 from . import decode as dec
-from . import latent_ops
+from . import latent_ops, vllm_plugin
 from .layer import LatentLayer
 
 BACKEND_NAME = "LRKV_LATENT"
@@ -36,7 +39,7 @@ PREFILL_CHUNK = int(os.environ.get("LRKV_PREFILL_CHUNK_TOKENS", 32768))
 SIDE_STREAM_MIN_DECODES = int(os.environ.get("LRKV_SIDE_STREAM_MIN_DECODES", 32))
 
 
-class AttentionType:
+class _StandInAttentionType:
     DECODER = "decoder"
     ENCODER = "encoder"
     ENCODER_ONLY = "encoder_only"
@@ -44,24 +47,41 @@ class AttentionType:
 
 
 @dataclass(frozen=True)
-class MultipleOf:
+class _StandInMultipleOf:
     base: int
 
 
-@dataclass(frozen=True, kw_only=True)
-class LatentKVSpec:
-    """One compressed layer's cache: a single head slot of ``head_size`` (the row width) elements per token and no
-    separate V (latent_backend.py:57-62)."""
+def make_kv_spec_class(api):
+    """``LatentKVSpec``: one compressed layer's cache, a single head slot of ``head_size`` (the row width) elements per
+    token and no separate V (latent_backend.py:57-62), on vLLM's ``FullAttentionSpec`` when ``api`` provides it."""
+    if api is not None:
+        @dataclass(frozen=True, kw_only=True)
+        class LatentKVSpec(api.FullAttentionSpec):
+            """One compressed layer's cache: one head slot of the row width per token, no separate V."""
 
-    block_size: int
-    num_kv_heads: int = 1
-    head_size: int = 0
-    dtype: torch.dtype = torch.bfloat16
-    head_size_v: int = 0
+            head_size_v: int = 0
+        return LatentKVSpec
 
-    @property
-    def page_size_bytes(self) -> int:
-        return self.block_size * self.num_kv_heads * self.head_size * torch.finfo(self.dtype).bits // 8
+    @dataclass(frozen=True, kw_only=True)
+    class LatentKVSpec:
+        """One compressed layer's cache: one head slot of the row width per token, no separate V."""
+
+        block_size: int
+        num_kv_heads: int = 1
+        head_size: int = 0
+        dtype: torch.dtype = torch.bfloat16
+        head_size_v: int = 0
+
+        @property
+        def page_size_bytes(self) -> int:
+            return self.block_size * self.num_kv_heads * self.head_size * torch.finfo(self.dtype).bits // 8
+    return LatentKVSpec
+
+
+_API = vllm_plugin.vllm_api()
+AttentionType = _API.AttentionType if _API is not None else _StandInAttentionType
+MultipleOf = _API.MultipleOf if _API is not None else _StandInMultipleOf
+LatentKVSpec = make_kv_spec_class(_API)
 
 
 @dataclass
@@ -347,49 +367,55 @@ def latent_attention_step(impl: "LatentAttentionImpl", layer, query: torch.Tenso
     return impl._attend(layer, query, kv_cache, m, output, side)
 
 
-class LatentAttentionBackend:
-    # the op writes the rows itself; False keeps vLLM padding the slot mapping to the token count of the key
-    forward_includes_kv_cache_update: bool = False
-    accept_output_buffer: bool = True
-    supported_dtypes: ClassVar[list] = [torch.bfloat16]
-    supported_kv_cache_dtypes: ClassVar[list] = ["auto", "bfloat16"]
+def make_backend_class(api):
+    """``LatentAttentionBackend`` (latent_backend.py:322-354) on vLLM's ``AttentionBackend`` when ``api`` provides it,
+    its block-size and layout types taken from the same API."""
+    base = api.AttentionBackend if api is not None else object
+    multiple_of = api.MultipleOf if api is not None else _StandInMultipleOf
+    layouts = (api.KVCacheLayout.BLHNC, api.KVCacheLayout.BLNHC) if api is not None else ("BLHNC", "BLNHC")
 
-    @staticmethod
-    def get_name() -> str:
-        return BACKEND_NAME
+    class LatentAttentionBackend(base):
+        # This backend writes the cache rows itself (inside forward); vLLM is told not to call a separate update, which
+        # also keeps the slot mapping padded to the key's token count, the layout the row-writing kernel reads.
+        forward_includes_kv_cache_update: bool = False
+        accept_output_buffer: bool = True
+        supported_dtypes: ClassVar[list] = [torch.bfloat16]
+        supported_kv_cache_dtypes: ClassVar[list] = ["auto", "bfloat16"]
 
-    @staticmethod
-    def get_impl_cls() -> type[LatentAttentionImpl]:
-        return LatentAttentionImpl
+        @staticmethod
+        def get_name() -> str:
+            return BACKEND_NAME
 
-    @staticmethod
-    def get_builder_cls() -> type[LatentAttentionMetadataBuilder]:
-        return LatentAttentionMetadataBuilder
+        @staticmethod
+        def get_impl_cls() -> type[LatentAttentionImpl]:
+            return LatentAttentionImpl
 
-    @staticmethod
-    def get_supported_kernel_block_sizes(kv_cache_spec=None) -> list:
-        # the decode kernel's tile is 128 tokens fetched as boxes of one page: 16, 32, 64 or a multiple of 128
-        return [16, 32, 64, MultipleOf(128)]
+        @staticmethod
+        def get_builder_cls() -> type[LatentAttentionMetadataBuilder]:
+            return LatentAttentionMetadataBuilder
 
-    @classmethod
-    def supports_head_size(cls, head_size: int) -> bool:
-        return True
+        @staticmethod
+        def get_supported_kernel_block_sizes(kv_cache_spec=None) -> list:
+            # the decode kernel's tile is 128 tokens fetched as boxes of one page: 16, 32, 64 or a multiple of 128
+            return [16, 32, 64, multiple_of(128)]
 
-    @classmethod
-    def supported_kv_cache_layouts(cls):
-        """Block-outermost only: the layers' row widths differ, so their pages share a block side by side."""
-        return ("BLHNC", "BLNHC")
+        @classmethod
+        def supports_head_size(cls, head_size: int) -> bool:
+            return True
+
+        @classmethod
+        def supported_kv_cache_layouts(cls):
+            """Block-major layouts only. Every compressed layer has its own row width, so the pages of one block sit
+            next to each other per layer, which needs the block index outermost."""
+            return layouts
+
+    return LatentAttentionBackend
+
+
+LatentAttentionBackend = make_backend_class(_API)
 
 
 def register_with_vllm() -> bool:
-    """Register the backend under ``LRKV_LATENT`` when the running vLLM exposes the attention-backend registry of the
-    plugin API the reference targets (vLLM 0.32); returns False when it does not."""
-    try:
-        from vllm.v1.attention.backends.registry import AttentionBackendEnum  # type: ignore
-    except Exception:
-        return False
-    try:
-        AttentionBackendEnum.register(BACKEND_NAME, f"{__name__}.LatentAttentionBackend")
-    except Exception:
-        return False
-    return True
+    """Register the backend under ``LRKV_LATENT`` (and the KV-cache hooks) in a vLLM that provides the plugin API the
+    reference targets; returns False when it does not (``vllm_plugin.register``)."""
+    return vllm_plugin.register()
