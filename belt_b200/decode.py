@@ -55,16 +55,17 @@ def _stream_ptr(device) -> int:
 
 @dataclass
 class DecodeSchedule:
-    """Device buffers of one step's work split, shared by all compressed layers of the step
-    (cute_decode.py:545-559).
+    """The split-KV work of one decode step, in device memory (interchangeable with the reference's buffers,
+    cute_decode.py:545-559). It is computed once per step and read by the decode and merge of every layer.
 
-    work [capacity, 4] int32: segment k = (request, first tile, end tile, 0), in request and tile order, so the
-    segments of request b are seg_base[b] .. seg_base[b + 1] - 1 and CTA c owns cta_seg[c] .. cta_seg[c + 1] - 1."""
+    ``work`` has one row per segment -- a run of consecutive tiles of one request -- holding (request, first tile,
+    end tile, unused); rows are sorted by request, then tile. ``seg_base[b]`` is the first row of request b (its rows
+    end at ``seg_base[b + 1]``), ``cta_seg[c]`` the first row CTA c processes (up to ``cta_seg[c + 1]``)."""
 
     num_ctas: int
-    work: torch.Tensor
-    cta_seg: torch.Tensor           # [num_ctas + 1] int32
-    seg_base: torch.Tensor          # [max_reqs + 1] int32
+    work: torch.Tensor              # [num_reqs + num_ctas, 4] int32 (the capacity)
+    cta_seg: torch.Tensor           # first segment row per CTA, plus the end: [num_ctas + 1] int32
+    seg_base: torch.Tensor          # first segment row per request, plus the end: [max_reqs + 1] int32
     # 0: the reference's split (equal runs of tiles); > 0: equal runs of cost, a tile costing 8 and a request's first
     # tile this much more (belt_decode_schedule_weighted)
     start_cost: int = 0

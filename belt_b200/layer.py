@@ -63,20 +63,6 @@ class LatentLayer:
         return latent_ops.decompress_paged(cache, block_table_row, seq_len, pos0, count, self.wk, self.k_segs_host,
                                            self.v_up, self.v_offset, self.rope.cos_sin, k_out, v_out)
 
-    def decompress(self, rows: torch.Tensor, positions: torch.Tensor):
-        """Cached rows [S, row_width] at text positions [S] -> the model's keys and values [S, G, head_dim] (RoPE
-        channels first), the reference's torch math (latent_backend.py:95-108). Used by the prefill path."""
-        rot = self.rotary_dim
-        rows = rows.to(self.qmap.dtype)
-        kc = min(self.n_k * CHUNK, rows.shape[1])
-        x = torch.einsum("sk,gdk->sgd", rows[:, :kc], self.rope_up[:, :, :kc]).float()
-        cos, sin = self.rope.cos_sin[positions].float().unsqueeze(1).chunk(2, dim=-1)
-        x1, x2 = x.chunk(2, dim=-1)
-        k_pe = torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(rows.dtype)
-        k_nope = torch.einsum("sk,gdk->sgd", rows[:, :kc], self.qmap[:, rot:, :kc])
-        v = torch.einsum("sr,grd->sgd", rows[:, self.v_offset:self.v_offset + self.v_rank], self.v_up)
-        return torch.cat((k_pe, k_nope), dim=-1), v
-
 
 def k_segs_rows(layout: dict) -> list:
     """[[start, length, start, length]] per group from the layout's ``k_segments`` (qwen3_5_latent.py:156-158)."""
