@@ -38,6 +38,9 @@ SIGNATURES = {
     "belt_q_norm_rope": [c_vp, c_i32, c_i64, c_i64, c_vp, c_f32, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_i64, c_i64,
                          c_vp],
     "belt_gate_mul": [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_i32, c_vp, c_i64, c_i64, c_vp],
+    "belt_merge_up_project": [c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp,
+                              c_vp],
+    "belt_gemm_bf16": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_selftest_bounded_wait": [c_vp, c_vp, c_vp],
     "belt_num_sms": [c_i32],
     "belt_abi_version": [],

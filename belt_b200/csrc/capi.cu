@@ -778,6 +778,73 @@ int belt_gate_mul(const void* attn, int64_t attn_st, int64_t attn_sh, const void
   return e == cudaSuccess ? ok() : cuda_fail(e, "gate_mul launch");
 }
 
+int belt_merge_up_project(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
+                          int32_t num_reqs, int32_t lv, const void* v_up_t, void* out, int64_t out_st, int64_t out_sh,
+                          float* lse, int64_t lse_sb, int32_t* err, void* stream) {
+  using namespace belt;
+  if (num_reqs < 0 || lv <= 0 || lv > 640)
+    return fail(BELT_ERR_INVALID, "merge_up_project: num_reqs %d, lv %d (at most 640)", num_reqs, lv);
+  if (num_reqs == 0) return ok();
+  if (!part || !seg_base || !v_up_t || !out) return fail(BELT_ERR_INVALID, "merge_up_project: null buffer");
+  if (part_sh < lv + 1 || part_ss < kH * part_sh || !aligned16(v_up_t) || (lse && lse_sb < kH))
+    return fail(BELT_ERR_INVALID, "merge_up_project: part strides, v_up_t alignment or lse stride");
+  MergeUpParams p{part, part_ss, part_sh, seg_base, num_reqs, kH, kHPG, lv, static_cast<__nv_bfloat16*>(out),
+                  out_st, out_sh, lse, lse_sb, err};
+  MergeUpMaps maps;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(lv), static_cast<cuuint64_t>(kG)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(lv) * kD * 2};
+  cuuint32_t box[3] = {64, 64, 1};
+  int r = encode_bf16(&maps.v, v_up_t, 3, dims, strides, box, "v_up_t");
+  if (r != BELT_OK) return r;
+  cudaError_t e = launch_merge_up(maps, p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "merge_up_project launch");
+}
+
+int belt_gemm_bf16(const void* a, int64_t m, int64_t k, int64_t lda, const void* b, int64_t n, int64_t ldb, void* c,
+                   int64_t ldc, int32_t* err, void* stream) {
+  using namespace belt;
+  if (m < 0 || n < 0 || k <= 0 || m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1)
+    return fail(BELT_ERR_INVALID, "gemm_bf16: m %lld, n %lld, k %lld", (long long)m, (long long)n, (long long)k);
+  if (m == 0 || n == 0) return ok();
+  if (!a || !b || !c) return fail(BELT_ERR_INVALID, "gemm_bf16: null buffer");
+  if (k % 8 || lda < k || ldb < k || lda % 8 || ldb % 8 || ldc < n || !aligned16(a) || !aligned16(b))
+    return fail(BELT_ERR_INVALID, "gemm_bf16: k %lld and the row strides (%lld, %lld) must be multiples of 8, a and b "
+                "16-byte aligned", (long long)k, (long long)lda, (long long)ldb);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  GemmParams p{};
+  p.c = static_cast<__nv_bfloat16*>(c);
+  p.ldc = ldc;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.tiles_m = static_cast<int>((m + 127) / 128);
+  // 256-column tiles when they still give every SM a tile, 128 otherwise (more, smaller tiles for small products)
+  const long long tiles256 = p.tiles_m * ((n + 255) / 256);
+  p.bn = tiles256 >= sms ? 256 : 128;
+  p.num_tiles = static_cast<int>(p.tiles_m * ((n + p.bn - 1) / p.bn));
+  p.vec_out = aligned16(c) && ldc % 8 == 0;
+  p.err = err;
+  GemmMaps maps;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda) * 2};
+    cuuint32_t box[2] = {64, 128};
+    int r = encode_bf16(&maps.a, a, 2, dims, strides, box, "gemm a");
+    if (r != BELT_OK) return r;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(n)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldb) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(p.bn)};
+    int r = encode_bf16(&maps.b, b, 2, dims, strides, box, "gemm b");
+    if (r != BELT_OK) return r;
+  }
+  cudaError_t e = launch_gemm(maps, p, sms, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "gemm_bf16 launch");
+}
+
 int belt_selftest_bounded_wait(int32_t* err, int32_t* status, void* stream) {
   if (!err || !status) return fail(BELT_ERR_INVALID, "selftest_bounded_wait: null buffer");
   cudaError_t e = belt::launch_selftest_wait(err, status, as_stream(stream));

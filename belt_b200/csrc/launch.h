@@ -118,6 +118,23 @@ struct MergeParams {
 };
 cudaError_t launch_merge(const MergeParams& p, cudaStream_t stream);
 
+// Segment merge + V up-projection (merge_up.cu): maps.v 3-D {256, r_v, G} over U_v^T [G, r_v, 256], box {64, 64, 1}.
+struct MergeUpMaps {
+  CUtensorMap v;
+};
+struct MergeUpParams {
+  const float* part;
+  long long ps, ph;
+  const int32_t* seg_base;
+  int num_reqs, nh, hpg, lv;
+  __nv_bfloat16* out;
+  long long sot, soh;
+  float* lse;          // may be null
+  long long slb;
+  int* err;
+};
+cudaError_t launch_merge_up(const MergeUpMaps& maps, const MergeUpParams& p, cudaStream_t stream);
+
 struct CacheWriteParams {
   const __nv_bfloat16* c;
   long long sct;
@@ -232,6 +249,24 @@ struct GateMulParams {
   long long out_st, out_sh;
 };
 cudaError_t launch_gate_mul(const GateMulParams& p, cudaStream_t stream);
+
+// Dense BF16 GEMM C = A B^T (gemm.cu): maps.a 2-D {K, M} box {64, 128}, maps.b 2-D {K, N} box {64, bn}, both with
+// the 128-byte swizzle; tiles of 128 x bn taken round-robin by a persistent grid.
+struct GemmMaps {
+  CUtensorMap a;
+  CUtensorMap b;
+};
+struct GemmParams {
+  __nv_bfloat16* c;
+  long long ldc;
+  int M, N, K;
+  int bn;                       // 128 or 256
+  int tiles_m, num_tiles;
+  int vec_out;                  // C rows 16-byte aligned
+  int stages;                   // set by the launcher
+  int* err;
+};
+cudaError_t launch_gemm(const GemmMaps& maps, GemmParams p, int num_sms, cudaStream_t stream);
 
 // Bounded-wait self-test (selftest.cu).
 cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);

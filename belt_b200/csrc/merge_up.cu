@@ -1,0 +1,209 @@
+// Segment merge and V up-projection in one kernel: the reference's ``merge_segments`` (plugins/vllm_lrkv/vllm_lrkv/
+// cute_decode.py:681-722) followed by ``up_project`` (latent_ops.py:76-81), with the merged latent output kept in
+// shared memory instead of a [B, H, r_v] buffer:
+//     a[b, h, :]   = bf16( sum_s exp(lse_s - m) part[s, h, :r_v] / sum_s exp(lse_s - m) )   over b's segments
+//     lse[b, h]    = m + log(sum_s exp(lse_s - m))                 (-inf and a zero output for a request without any)
+//     out[b, h, :] = bf16( U_v,g(h) a[b, h, :] )                   (FP32 accumulation)
+// The roundings are the unfused path's (a rounded to BF16 before the projection), so the two agree to one BF16 ulp.
+//
+// One CTA per (head, tile of 32 requests), 128 threads:
+//   * thread 0 streams U_v^T of the head's group ([r_v, 256], channels contiguous) in 64-deep K blocks, four boxes of
+//     64 channels x 64 k (MN-major, 128-byte swizzle) per stage, from the start (it does not depend on the merge);
+//   * all warps merge: warp w takes requests w, w + 4, ..; the lanes reduce the segment LSEs, then sweep the r_v
+//     features (coalesced rows of part) and write a as the K-major B operand (32 requests x r_v, 128-byte swizzle);
+//   * thread 32 issues tcgen05 out^T[channel, request] += U_v^T[channel, k] a^T[k, request]: M = 128 channels (two
+//     halves), N = 32 requests, K = 16 per instruction, into TMEM;
+//   * epilogue: thread (warp w, lane l) holds channel 32 w + l of both halves for the 32 requests; a warp's stores of
+//     one request cover 32 consecutive channels (64 bytes).
+#include "common.cuh"
+#include "launch.h"
+
+namespace belt {
+
+namespace {
+constexpr int kMuThreads = 128;
+constexpr int kMuReqs = 32;                         // requests per CTA (the MMA's N)
+constexpr int kMuStageBytes = 4 * 64 * 128;         // 256 channels x 64 k x 2 B = 32 KB
+constexpr int kMuStages = 3;
+constexpr int kMuMaxChunks = 10;                    // r_v <= 640
+constexpr int kMuBChunk = kMuReqs * 128;            // 32 requests x 64 k x 2 B = 4 KB per K block
+constexpr int kMuOffB = kMuStages * kMuStageBytes;  // 96 KB
+constexpr int kMuOffW = kMuOffB + kMuMaxChunks * kMuBChunk;   // per-warp segment weights
+constexpr int kMuWeights = 256;                     // segment weights staged per pass, per warp
+constexpr int kMuOffBars = kMuOffW + 4 * kMuWeights * 4;
+// barriers: full[3], empty[3], done
+constexpr int uFull = 0, uEmpty = 3, uDone = 6, kMuBars = 7;
+
+// Offset of element (row, k) of a K-major 128-byte-swizzled operand of 64-column chunks of `rows` rows.
+__device__ __forceinline__ int sw128_elem(int row, int k, int rows) {
+  const int c = k >> 6, kk = k & 63;
+  return c * rows * 128 + row * 128 + ((((kk >> 3) ^ (row & 7)) << 4) | ((kk & 7) << 1));
+}
+}  // namespace
+
+__global__ void __launch_bounds__(kMuThreads, 1)
+    merge_up_kernel(const __grid_constant__ MergeUpMaps maps, const __grid_constant__ MergeUpParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = smem + kMuOffB;
+  float* wts_all = reinterpret_cast<float*>(smem + kMuOffW);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kMuOffBars);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kMuBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, b0 = blockIdx.y * kMuReqs, g = h / p.hpg;
+  const int nk = (p.lv + 63) / 64;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMuBars; ++i) mbar_init(&bars[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&maps.v);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // ---------------------------------------------------------------- producer: the first stages, before the merge
+  int issued = 0;
+  auto produce = [&](int k) {   // thread 0 only; k < kMuStages needs no wait
+    const int s = k % kMuStages;
+    uint8_t* st = smem + s * kMuStageBytes;
+    mbar_arrive_expect_tx(&bars[uFull + s], kMuStageBytes);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 8192, &maps.v, &bars[uFull + s], 64 * q, 64 * k, g);
+  };
+  if (threadIdx.x == 0)
+    for (; issued < nk && issued < kMuStages; ++issued) produce(issued);
+
+  // ---------------------------------------------------------------- merge into the B operand
+  // zero the operand first: feature columns past r_v must be 0 (U_v's zero-filled rows meet them)
+  for (int i = threadIdx.x; i < nk * kMuBChunk / 16; i += kMuThreads)
+    reinterpret_cast<uint4*>(sB)[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  float* wts = wts_all + warp * kMuWeights;
+  for (int j = warp; j < kMuReqs; j += 4) {
+    const int b = b0 + j;
+    if (b >= p.num_reqs) break;
+    const int s0 = __ldg(p.seg_base + b), n = __ldg(p.seg_base + b + 1) - s0;
+    const float* base = p.part + static_cast<long long>(s0) * p.ps + static_cast<long long>(h) * p.ph;
+    float m = -INFINITY;
+    for (int s = lane; s < n; s += 32) m = fmaxf(m, __ldg(base + static_cast<long long>(s) * p.ps + p.lv));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float den = 0.f;
+    for (int s = lane; s < n; s += 32) den += __expf(__ldg(base + static_cast<long long>(s) * p.ps + p.lv) - m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    const bool has = den > 0.f;
+    const float inv = has ? 1.f / den : 0.f;
+    if (lane == 0 && p.lse) p.lse[static_cast<long long>(b) * p.slb + h] = has ? m + __logf(den) : -INFINITY;
+    for (int f0 = 0; f0 < p.lv; f0 += 32 * 8) {
+      float acc[8] = {};
+      for (int sw = 0; sw < n; sw += kMuWeights) {
+        const int cnt = min(kMuWeights, n - sw);
+        __syncwarp();
+        for (int i = lane; i < cnt; i += 32)
+          wts[i] = __expf(__ldg(base + static_cast<long long>(sw + i) * p.ps + p.lv) - m);
+        __syncwarp();
+        for (int i = 0; i < cnt; ++i) {
+          const float w = wts[i];
+          const float* row = base + static_cast<long long>(sw + i) * p.ps;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int f = f0 + 32 * q + lane;
+            if (f < p.lv) acc[q] = fmaf(w, __ldg(row + f), acc[q]);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int f = f0 + 32 * q + lane;
+        if (f < p.lv)
+          *reinterpret_cast<__nv_bfloat16*>(sB + sw128_elem(j, f, kMuReqs)) = __float2bfloat16_rn(acc[q] * inv);
+      }
+    }
+  }
+  fence_proxy_async_smem();   // the operand's generic-proxy stores, before the tensor core reads them
+  __syncthreads();
+
+  // ---------------------------------------------------------------- MMA (thread 32) and the remaining stages (thread 0)
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (; ok && issued < nk; ++issued) {
+      const int s = issued % kMuStages;
+      if (!(ok = mbar_wait(&bars[uEmpty + s], ((issued / kMuStages) - 1) & 1, abort_flag, p.err,
+                           kErrTimeoutProducer)))
+        break;
+      produce(issued);
+    }
+    if (*abort_flag)
+      for (int k = issued > kMuStages ? issued - kMuStages : 0; k < issued; ++k)
+        mbar_wait_bounded(&bars[uFull + k % kMuStages], (k / kMuStages) & 1, nullptr, 0, kWaitCycles / 8);
+  } else if (threadIdx.x == 32) {
+    constexpr uint32_t idesc = idesc_bf16(128, kMuReqs, 1, 0);   // A (U_v^T) MN-major, B (a) K-major
+    constexpr uint32_t hiA = desc_hi(1024, kSwizzle128);          // 8 k rows of 128 bytes
+    constexpr uint32_t hiB = desc_hi(1024, kSwizzle128);          // 8 request rows
+    const uint32_t base = smem_u32(smem), b_base = smem_u32(sB);
+    bool ok = true;
+    for (int k = 0; k < nk && ok; ++k) {
+      const int s = k % kMuStages;
+      if (!(ok = mbar_wait(&bars[uFull + s], (k / kMuStages) & 1, abort_flag, p.err, kErrTimeoutMma))) break;
+      tc_fence_after();
+      const uint32_t st = base + s * kMuStageBytes;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t db = desc_of(desc_lo(b_base + k * kMuBChunk, 16) + 2 * kk, hiB);
+#pragma unroll
+        for (int half = 0; half < 2; ++half)   // channels [128 half, 128 half + 128): two 64-channel blocks
+          mma_ss(tmem + 32 * half, desc_of(desc_lo(st + half * 16384, 8192) + kk * (2048 >> 4), hiA), db, idesc,
+                 (k | kk) != 0 ? 1u : 0u);
+      }
+      mma_commit(&bars[uEmpty + s]);
+    }
+    if (!ok) *abort_flag = 1;
+    mma_commit(&bars[uDone]);   // arrives once every MMA issued has completed
+  }
+  __syncwarp();
+
+  // ---------------------------------------------------------------- epilogue
+  const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[uDone], 0, p.err, kErrTimeoutEpilogue));
+  tc_fence_after();
+  if (done && !*abort_flag) {
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + 32 * half, r);
+      tmem_ld_wait();
+      const int ch = 128 * half + 32 * warp + lane;
+#pragma unroll
+      for (int j = 0; j < kMuReqs; ++j) {
+        const int b = b0 + j;
+        if (b < p.num_reqs)
+          p.out[static_cast<long long>(b) * p.sot + static_cast<long long>(h) * p.soh + ch] =
+              __float2bfloat16_rn(__uint_as_float(r[j]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+cudaError_t launch_merge_up(const MergeUpMaps& maps, const MergeUpParams& p, cudaStream_t stream) {
+  if (p.num_reqs == 0) return cudaSuccess;
+  const int smem = 1024 + kMuOffBars + kMuBars * 8 + 16;
+  cudaError_t e = cudaFuncSetAttribute(merge_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.nh, (p.num_reqs + kMuReqs - 1) / kMuReqs);
+  merge_up_kernel<<<grid, kMuThreads, smem, stream>>>(maps, p);
+  return cudaGetLastError();
+}
+
+}  // namespace belt

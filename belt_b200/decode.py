@@ -195,3 +195,21 @@ def merge_segments(part: torch.Tensor, sched: DecodeSchedule, out: torch.Tensor,
     if lse.dtype != torch.float32 or lse.stride(-1) != 1:
         raise ValueError("merge_segments: lse must be fp32 [B, H]")
     torch.ops.lrkv_b200.merge_segments(part, sched.seg_base, out, lse)
+
+
+def merge_up_project(part: torch.Tensor, sched: DecodeSchedule, v_up_t: torch.Tensor, out: torch.Tensor,
+                     lse: torch.Tensor) -> None:
+    """``merge_segments`` and the V up-projection in one kernel: part [segments, H, lv + 1] -> out [B, H, 256] (BF16,
+    written in place, e.g. the first rows of the attention output) = U_v,g(h) bf16(merged a), and lse [B, H] (fp32).
+    The merged output never leaves the chip; the roundings are those of ``merge_segments`` + ``up_project``."""
+    B, nh, D = out.shape
+    lv = v_up_t.shape[1]
+    if part.dtype != torch.float32 or part.stride(-1) != 1 or part.shape[-1] != lv + 1:
+        raise ValueError("merge_up_project: part must be fp32 [segments, H, lv + 1] with a contiguous last dim")
+    if out.dtype != torch.bfloat16 or out.stride(-1) != 1 or nh != H or D != 256:
+        raise ValueError("merge_up_project: out must be BF16 [B, 24, 256] with contiguous channels")
+    if v_up_t.dtype != torch.bfloat16 or not v_up_t.is_contiguous() or v_up_t.shape[0] != G or v_up_t.shape[2] != 256:
+        raise ValueError("merge_up_project: v_up_t must be a contiguous BF16 [4, lv, 256]")
+    if lse.dtype != torch.float32 or lse.stride(-1) != 1 or lse.shape[0] < B:
+        raise ValueError("merge_up_project: lse must be fp32 [B, H]")
+    torch.ops.lrkv_b200.merge_up_project(part, sched.seg_base, v_up_t, out, lse)

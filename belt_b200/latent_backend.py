@@ -301,12 +301,11 @@ class LatentAttentionImpl:
                 side = None
             part = torch.empty(nd + m.sched.num_ctas, self.num_heads, lat.v_rank + 1, dtype=torch.float32,
                                device=dev)
-            a = torch.empty(nd, self.num_heads, lat.v_rank, dtype=query.dtype, device=dev)
             lse = torch.empty(nd, self.num_heads, dtype=torch.float32, device=dev)
             dec.latent_decode(q_bd, cache, m.block_table[:nd], m.seq_lens[:nd], m.sched, part, self.scale,
                               lat.v_offset, lat.v_rank, rope=lat.rope)
-            dec.merge_segments(part, m.sched, a, lse)
-            lat.up_project(a, output[:nd])
+            # the segment merge and the U_v projection in one kernel, straight into the output rows
+            dec.merge_up_project(part, m.sched, lat.v_up, output[:nd], lse)
         if side is not None:
             torch.cuda.current_stream(query.device).wait_stream(side)
         if m.num_prefills:

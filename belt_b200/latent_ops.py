@@ -103,9 +103,20 @@ def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: tor
     torch.ops.lrkv_b200.cache_write(c, slot_mapping, cache, u_cat, segs, float(eps))
 
 
-# From this many tokens on (prefill chunks) the projection runs as a library GEMM followed by the cache write: the fused
-# kernel re-streams W_down for every 128 tokens, which costs more than the round trip of c (8192 tokens: 52 against
-# 66 us); below it the fused kernel is as fast and needs no buffer for c.
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """x [M, K] @ weight[N, K]^T on the tensor cores (``belt_gemm_bf16``): BF16 operands with contiguous rows (any row
+    strides that are multiples of 8), FP32 accumulation, BF16 out [M, N]. The model's linear layers (q_gate_proj,
+    o_proj, kv_latent_proj at prefill sizes)."""
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError(f"linear: x {tuple(x.shape)} and weight {tuple(weight.shape)} ([M, K] and [N, K])")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or x.stride(1) != 1 or weight.stride(1) != 1:
+        raise ValueError("linear: BF16 x and weight with contiguous rows")
+    return torch.ops.lrkv_b200.linear(x, weight)
+
+
+# From this many tokens on (prefill chunks) the projection runs as a GEMM (``linear``) followed by the cache write: the
+# fused kernel re-streams W_down for every 128 tokens, which costs more than the round trip of c (8192 tokens); below
+# it the fused kernel is as fast and needs no buffer for c.
 FUSED_WRITE_MAX_TOKENS = 2048
 
 
@@ -114,7 +125,8 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
     """``latent_rows_to_cache(bf16(x @ w_down^T), ...)``: x [T, hidden] BF16 (the layer inputs of the new tokens),
     w_down [>= W, hidden] BF16 (``kv_latent_proj.weight``, zero rows at the gaps), the other arguments as
     ``latent_rows_to_cache``. ``fused`` (default: fewer than FUSED_WRITE_MAX_TOKENS tokens) runs it as one kernel that
-    never materialises the projection; otherwise the projection is a library GEMM into a [T, W] buffer."""
+    never materialises the projection; otherwise the projection is this package's GEMM (``linear``) into a [T, W]
+    buffer, then the cache write."""
     T = slot_mapping.shape[0]
     if T == 0:
         return
@@ -133,7 +145,7 @@ def project_rows_to_cache(x: torch.Tensor, w_down: torch.Tensor, slot_mapping: t
     if fused is None:
         fused = T < FUSED_WRITE_MAX_TOKENS
     if not fused:
-        latent_rows_to_cache(x[:T] @ w_down[:W].T, slot_mapping, cache, u_cat, k_segs, eps)
+        latent_rows_to_cache(linear(x[:T], w_down[:W]), slot_mapping, cache, u_cat, k_segs, eps)
         return
     torch.ops.lrkv_b200.proj_cache_write(x, w_down, slot_mapping, cache, u_cat, segs, float(eps))
 

@@ -1,12 +1,12 @@
 """The attention block of a compressed layer as the model runs it (plugins/vllm_lrkv/vllm_lrkv/models/
 qwen3_5_latent.py:98-217, ``LatentAttention`` + ``forward``), on this package's kernels:
 
-    qg   = hidden @ q_gate_proj^T                         [T, 24 * 2 * 256]   (a plain GEMM, cuBLAS)
+    qg   = hidden @ q_gate_proj^T                         [T, 24 * 2 * 256]   belt_gemm_bf16 (tcgen05)
     q    = NeoX-RoPE(RMSNorm_{1 + w}(qg query halves))     belt_q_norm_rope    (the query side of the fused q-norm/RoPE)
     rows = the new tokens' cache rows from hidden            fused into the cache write (belt_latent_proj_rows_to_cache)
     attn = the backend's decode / prefill attention          ``latent_attention_step``
     attn = attn * sigmoid(qg gate halves)                    belt_gate_mul
-    out  = attn @ o_proj^T                                   (a plain GEMM, cuBLAS)
+    out  = attn @ o_proj^T                                   belt_gemm_bf16 (tcgen05)
 
 One model copy per GPU (the reference refuses tensor parallelism, qwen3_5_latent.py:101-102). The weights are the
 export's: ``q_gate_proj`` [24 * 512, hidden], ``o_proj`` [hidden, 24 * 256], ``q_norm`` / ``k_norm`` weights [256]
@@ -20,6 +20,7 @@ import torch
 from . import _lib
 from .decode import _stream_ptr
 from .latent_backend import LatentAttentionImpl, LatentAttentionMetadata, latent_attention_step
+from .latent_ops import linear
 from .layer import derive_latent_tensors
 
 H, D = 24, 256
@@ -84,9 +85,9 @@ class LatentSelfAttention:
     def forward(self, positions: torch.Tensor, hidden: torch.Tensor, kv_cache: torch.Tensor,
                 attn_metadata: LatentAttentionMetadata) -> torch.Tensor:
         T = hidden.shape[0]
-        qg = (hidden @ self.q_gate_proj.T).view(T, H, 2 * D)
+        qg = linear(hidden, self.q_gate_proj).view(T, H, 2 * D)
         q = q_norm_rope(qg[:, :, :D], self.q_norm_weight, self.eps, self.latent.rope.cos_sin, positions)
         attn = torch.empty(T, H, D, dtype=torch.bfloat16, device=hidden.device)
         latent_attention_step(self.impl, self, q, hidden, self.kv_latent_proj, kv_cache, attn_metadata, attn)
         gate_mul(attn, qg[:, :, D:], out=attn)
-        return attn.view(T, H * D) @ self.o_proj.T
+        return linear(attn.view(T, H * D), self.o_proj)

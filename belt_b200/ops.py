@@ -20,10 +20,12 @@ Operators (mutated arguments marked !):
   latent_decode(q_bd, cache, block_table, seq_lens, work, cta_seg, part!, num_ctas, sm_scale, lk_pad, lv,
                 rope_groups, rope_blocks, cos_sin)
   merge_segments(part, seg_base, out!, lse!)
+  merge_up_project(part, seg_base, v_up_t, out!, lse!)
   block_diag_query(q, qmap, col_runs) -> q_bd
   up_project(a, v_up_t, out!)
   decompress(cache, block_table_row, seq_len, pos0, wk, k_segs, v_up_t, v_offset, cos_sin, k_out!, v_out!)
   prefill_attention(q, k, v, q_pos0, k_pos0, scale, causal, out!, lse!)
+  linear(x, weight) -> x weight^T  (the model's linear layers, BF16)
 """
 
 from __future__ import annotations
@@ -133,6 +135,21 @@ def _(part, seg_base, out, lse):
     return None
 
 
+@custom_op(f"{NS}::merge_up_project", mutates_args=("out", "lse"), device_types="cuda")
+def merge_up_project(part: torch.Tensor, seg_base: torch.Tensor, v_up_t: torch.Tensor, out: torch.Tensor,
+                     lse: torch.Tensor) -> None:
+    B = out.shape[0]
+    lv = v_up_t.shape[1]
+    _lib.call("belt_merge_up_project", part.data_ptr(), part.stride(0), part.stride(1), seg_base.data_ptr(), B, lv,
+              v_up_t.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0),
+              _err(part), _stream(out))
+
+
+@merge_up_project.register_fake
+def _(part, seg_base, v_up_t, out, lse):
+    return None
+
+
 # ------------------------------------------------------------------------------------------ per-head projections
 @custom_op(f"{NS}::block_diag_query", mutates_args=(), device_types="cuda")
 def block_diag_query(q: torch.Tensor, qmap: torch.Tensor, col_runs: list[int]) -> torch.Tensor:
@@ -191,5 +208,22 @@ def _(q, k, v, q_pos0, k_pos0, scale, causal, out, lse):
     return None
 
 
-OPS = ("cache_write", "proj_cache_write", "decode_schedule", "latent_decode", "merge_segments", "block_diag_query",
-       "up_project", "decompress", "prefill_attention")
+# ---------------------------------------------------------------------------------------------------------- linear
+@custom_op(f"{NS}::linear", mutates_args=(), device_types="cuda")
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    M, K = x.shape
+    N = weight.shape[0]
+    out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    _lib.call("belt_gemm_bf16", x.data_ptr(), M, K, x.stride(0), weight.data_ptr(), N, weight.stride(0),
+              out.data_ptr(), out.stride(0), _err(x), _stream(x))
+    return out
+
+
+@linear.register_fake
+def _(x, weight):
+    return x.new_empty(x.shape[0], weight.shape[0])
+
+
+OPS = ("cache_write", "proj_cache_write", "decode_schedule", "latent_decode", "merge_segments", "merge_up_project",
+       "block_diag_query",
+       "up_project", "decompress", "prefill_attention", "linear")

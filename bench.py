@@ -10,8 +10,8 @@ from {384, 448, 512, 576, 640}, r_v = 1024 - r_k, row width 1024), batch 128, co
 CPU-runnable case (4 requests, one layer; for the reference arm).
 
 A step is one decode step of the path over the batch: the split-KV schedule once, then per layer the cache write of
-the new token's row, the absorbed block-diagonal query, the decode kernel, the segment merge and the U_v
-up-projection. ``value`` is whole-job decode tokens/s (sequences x GPUs / step time, device-timed with CUDA events,
+the new token's row, the absorbed block-diagonal query, the decode kernel, and the segment merge with the U_v
+up-projection (one kernel). ``value`` is whole-job decode tokens/s (sequences x GPUs / step time, device-timed with CUDA events,
 max over ranks); the cache (tens of GB) is far larger than L2, so every step streams it from HBM. ``e2e`` runs the same
 step through the backend's public API (``LatentAttentionImpl.forward``) from pinned host buffers: this step's queries
 and latent rows are copied in and the attention outputs copied out inside the timed region.
@@ -77,6 +77,8 @@ def parse_args():
     ap.add_argument("--decode-steps", type=int, default=256, help="config 5: decode steps per wave")
     ap.add_argument("--prefill-chunk", type=int, default=8192, help="config 5: tokens per chunked-prefill write")
     ap.add_argument("--num-seqs", type=int, default=1024, help="config 5: sequences on the box")
+    ap.add_argument("--gemm", action="store_true",
+                    help="measure the tensor-core GEMM on the model's linear-layer shapes instead (one GPU)")
     ap.add_argument("--prefill", action="store_true",
                     help="measure the prefill path instead (one GPU): keys / values rebuilt from the paged rows and "
                          "causal attention of 8192 new tokens over an 8192-token context, one c50 layer")
@@ -165,7 +167,6 @@ class Workload:
         self.sched = dec.make_schedule(self.B, device)
         self.side = torch.cuda.Stream(device)
         self.part = torch.empty(self.B + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
-        self.a = torch.empty(self.B, H, 640, dtype=torch.bfloat16, device=device)
         self.lse = torch.empty(self.B, H, dtype=torch.float32, device=device)
         self.out = torch.empty(self.L, self.B, H, D, dtype=torch.bfloat16, device=device)
 
@@ -190,11 +191,9 @@ class Workload:
                               lat.v_offset, lat.v_rank, rope=lat.rope)
             if dec_events is not None:
                 dec_events[l][1].record()
-            a = self.a[:, :, :lat.v_rank]
-            dec.merge_segments(part, self.sched, a, self.lse)
-            lat.up_project(a, self.out[l])
+            dec.merge_up_project(part, self.sched, lat.v_up, self.out[l], self.lse)
 
-    launches_per_step = property(lambda self: 1 + 5 * self.L)
+    launches_per_step = property(lambda self: 1 + 4 * self.L)
 
     # ------------------------------------------------------------------------------------------------ algorithmic units
     def decode_kernel_bytes(self, l: int) -> int:
@@ -562,6 +561,68 @@ def read_traffic():
         return None
 
 
+GEMM_SHAPES = [
+    # (name, M, N, K): the model's linear layers at hidden 1024, and one large product for the peak comparison
+    ("kv_latent_proj, 8192-token prefill chunk", 8192, 1024, 1024),
+    ("q_gate_proj, 8192-token prefill chunk", 8192, 12288, 1024),
+    ("o_proj, 8192-token prefill chunk", 8192, 1024, 6144),
+    ("q_gate_proj, 128-token decode step", 128, 12288, 1024),
+    ("square 8192", 8192, 8192, 8192),
+]
+
+
+def run_gemm(args):
+    """TFLOP/s of ``latent_ops.linear`` (the tcgen05 GEMM) on the model's shapes, CUDA events around each launch with
+    L2 flushed before it, torch's matmul (cuBLAS) on the same operands beside; one JSON line (the first shape's figures
+    at the top level, every shape under ``shapes``)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from belt_b200 import build as _build
+    _build.build()
+    peaks = load_peaks()
+    peak_tf = peaks.get("bf16_tflops") or 1590.0
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    rows = []
+    clocks = ClockSampler(dev)
+    clocks.start()
+    for name, M, N, K in GEMM_SHAPES:
+        g = torch.Generator(device=dev).manual_seed(M + N + K)
+        x = torch.randn(M, K, generator=g, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(N, K, generator=g, device=dev, dtype=torch.bfloat16) / K ** 0.5
+
+        def timed(fn):
+            for _ in range(max(args.warmup, 3)):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+            for s_, e_ in ev:
+                flush.add_(1)
+                s_.record()
+                fn()
+                e_.record()
+            torch.cuda.synchronize()
+            return statistics.median(s_.elapsed_time(e_) for s_, e_ in ev)
+
+        ms = timed(lambda: latent_ops.linear(x, w))
+        lib_ms = timed(lambda: x @ w.T)
+        err = float((latent_ops.linear(x, w).float() - (x @ w.T).float()).abs().max())
+        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        rows.append({"shape": name, "M": M, "N": N, "K": K, "ms": ms, "tflops": tf, "frac": tf / peak_tf,
+                     "library_ms": lib_ms, "library_tflops": 2.0 * M * N * K / (lib_ms / 1e3) / 1e12,
+                     "max_abs_diff_vs_library": err})
+    clk = clocks.stop()
+    dec.check_device_errors(dev)
+    top = rows[0]
+    line = {"metric": "tensor-core GEMM TFLOP/s (model linear layers)", "value": top["tflops"], "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": top["ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": top["shape"], "l2": "flushed (256 MB write) before every timed launch"},
+            "roofline": {"bound": "tensor", "achieved": top["tflops"], "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": top["frac"], "peak_source": "measured" if "bf16_tflops" in peaks else "fallback"},
+            "shapes": rows, "clocks": clk, "gpu_launches": len(rows) * (args.steps + max(args.warmup, 3) + 1)}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill(args):
     """One c50 layer's prefill of an 8192-token request through the backend's kernels: decompress of the context
     (keys and values from the paged rows) and the causal attention, timed on the device (inputs resident, L2 flushed
@@ -718,7 +779,6 @@ class ServingRun:
         self.xp = torch.randn(4, chunk, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
         self.sched = dec.make_schedule(Bmax, device)
         self.part = torch.empty(Bmax + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
-        self.a = torch.empty(Bmax, H, 640, dtype=torch.bfloat16, device=device)
         self.lse = torch.empty(Bmax, H, dtype=torch.float32, device=device)
         self.out = torch.empty(self.L, Bmax, H, D, dtype=torch.bfloat16, device=device)
         self.side = torch.cuda.Stream(device)
@@ -757,9 +817,7 @@ class ServingRun:
             part = self.part[:B + self.sched.num_ctas, :, :lat.v_rank + 1]
             dec.latent_decode(q_bd, cache, m["block_table"], seq_lens, self.sched, part, SCALE, lat.v_offset,
                               lat.v_rank, rope=lat.rope)
-            a = self.a[:B, :, :lat.v_rank]
-            dec.merge_segments(part, self.sched, a, self.lse[:B])
-            lat.up_project(a, self.out[l, :B])
+            dec.merge_up_project(part, self.sched, lat.v_up, self.out[l, :B], self.lse[:B])
 
     def prefill_chunk(self, k, c):
         m = self.meta[k]
@@ -792,7 +850,7 @@ class ServingRun:
         """This repository's kernel launches in ``run`` (the prefill chunks' projection GEMM is a library call and is
         counted apart, in ``library_gemm_launches``)."""
         dec_steps = len(self.waves) * self.steps
-        return dec_steps * (1 + 5 * self.L) + sum(m["chunks"] for m in self.meta) * self.L
+        return dec_steps * (1 + 4 * self.L) + sum(m["chunks"] for m in self.meta) * self.L
 
 
 def run_serving(args, group, dev):
@@ -873,6 +931,10 @@ def main():
     if args.prefill:
         if rank == 0:
             run_prefill(args)
+        return
+    if args.gemm:
+        if rank == 0:
+            run_gemm(args)
         return
     group = dp.HostGroup()
     local = group.local_rank

@@ -142,6 +142,18 @@ int belt_merge_segments(const float* part, int64_t part_ss, int64_t part_sh, con
                         float* lse, int64_t lse_sb, void* stream);
 
 /*
+ * Segment merge and V up-projection in one kernel: belt_merge_segments followed by belt_up_project (cute_decode.py:
+ * 715-722 `merge_segments`, then latent_ops.py:76-81 `up_project`), with the merged latent output kept on chip.
+ * part [segments, 24, lv + 1] fp32 (strides part_ss, part_sh; last dim contiguous), seg_base [num_reqs + 1] int32,
+ * v_up_t [4, lv, 256] BF16 contiguous (U_v transposed) -> out [num_reqs, 24, 256] BF16 (strides out_st, out_sh, 1),
+ * lse [num_reqs, 24] fp32 (row stride lse_sb; may be NULL). The merged output is rounded to BF16 before the
+ * projection, as the two-kernel path does; lv <= 640. err: optional device error word.
+ */
+int belt_merge_up_project(const float* part, int64_t part_ss, int64_t part_sh, const int32_t* seg_base,
+                          int32_t num_reqs, int32_t lv, const void* v_up_t, void* out, int64_t out_st, int64_t out_sh,
+                          float* lse, int64_t lse_sb, int32_t* err, void* stream);
+
+/*
  * One decode step of a compressed layer with no caller-provided scratch: belt_decode_schedule_weighted (start cost
  * 10, the backend's split), belt_latent_decode and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
  * 24 MiB array inside this library instead of buffers from the caller. It has no counterpart in the reference
@@ -196,6 +208,16 @@ int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh
                            int32_t num_keys, int64_t kv_st, int64_t kv_sg, int32_t q_pos0, int32_t k_pos0,
                            int32_t causal, float scale, void* out, int64_t out_st, int64_t out_sh, float* lse,
                            int64_t lse_st, int32_t* err, void* stream);
+
+/*
+ * Dense BF16 GEMM on the tensor cores: c[M, N] = a[M, K] b[N, K]^T (both K-major: a row-major with row stride lda, b
+ * row-major [N, K] with row stride ldb, the layout of a torch Linear weight), FP32 accumulation, BF16 out (row stride
+ * ldc). Replaces the model's linear layers around the latent attention (models/qwen3_5_latent.py:130-140, 204-217:
+ * q_gate_proj, o_proj, and kv_latent_proj where the prefill computes the latent rows). K, lda, ldb multiples of 8;
+ * a, b 16-byte aligned. err: optional device word for a wait that timed out.
+ */
+int belt_gemm_bf16(const void* a, int64_t m, int64_t k, int64_t lda, const void* b, int64_t n, int64_t ldb, void* c,
+                   int64_t ldc, int32_t* err, void* stream);
 
 /*
  * The query side of the model's fused q-norm / RoPE (models/qwen3_5_latent.py:209-212, `fused_qk_rmsnorm_rope_gate`

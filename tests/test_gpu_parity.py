@@ -317,6 +317,41 @@ def test_merge_segments():
         assert torch.allclose(lse.cpu()[live], el[live], atol=1e-4)
 
 
+def test_merge_up_project():
+    """The fused merge + U_v projection against the two-kernel path (within 1 BF16 ulp: the same roundings, another
+    FP32 summation order in the projection) and against the oracle's merge followed by its projection (2 ulp)."""
+    g = torch.Generator().manual_seed(3)
+    long = [int(x) for x in torch.randint(1, 3000, (70,), generator=g)]
+    for seqs, nct, lv in [([129, 513, 1025, 2001], 16, 512), ([0, 300, 64, 0], 8, 96), ([40] * 40, 8, 640),
+                          ([9000] * 3, 148, 384), ([300 * 128], 300, 64), (long, 148, 576), ([17, 5, 900], 4, 300)]:
+        B = len(seqs)
+        sched = dec.make_schedule(B, DEV, num_ctas=nct)
+        dec.schedule(sched, torch.tensor(seqs, dtype=torch.int32, device=DEV))
+        nseg = int(sched.seg_base[B])
+        part = torch.randn(nseg + 1, 24, lv + 1, generator=g)
+        part[:, :, lv] *= 4
+        v_up_t = (torch.randn(4, lv, 256, generator=g) / lv ** 0.5).to(torch.bfloat16)
+        part_d, v_d = part.to(DEV), v_up_t.to(DEV)
+        out = torch.full((B, 24, 256), float("nan"), dtype=torch.bfloat16, device=DEV)
+        lse = torch.full((B, 24), float("nan"), device=DEV)
+        dec.merge_up_project(part_d, sched, v_d, out, lse)
+        a2 = torch.empty(B, 24, lv, dtype=torch.bfloat16, device=DEV)
+        lse2 = torch.empty(B, 24, device=DEV)
+        dec.merge_segments(part_d, sched, a2, lse2)
+        out2 = torch.empty(B, 24, 256, dtype=torch.bfloat16, device=DEV)
+        latent_ops.up_project(a2, v_d, out2)
+        torch.cuda.synchronize()
+        dec.check_device_errors(DEV)
+        what = f"{B} requests, {nct} CTAs, lv {lv}"
+        assert bf16_ulp_close(out.cpu(), out2.cpu(), ulps=1, atol=1e-5), what
+        assert torch.equal(torch.isinf(lse.cpu()), torch.isinf(lse2.cpu())), what
+        live = torch.isfinite(lse2.cpu())
+        assert torch.allclose(lse.cpu()[live], lse2.cpu()[live], atol=1e-6, rtol=0), what
+        ea, el = oracle.merge_segments(part, sched.seg_base.cpu(), B, lv)
+        eo = oracle.up_project(ea.to(torch.bfloat16), v_up_t)
+        assert bf16_ulp_close(out.cpu(), eo, ulps=2, atol=1e-5), what
+
+
 # ------------------------------------------------------------------------------------------------- decode
 @pytest.mark.parametrize("name", CASES)
 @pytest.mark.parametrize("num_ctas", [148, 7, 1])
