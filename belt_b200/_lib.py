@@ -33,6 +33,12 @@ SIGNATURES = {
                                    c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_latent_decompress": [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_vp, c_i32,
                                c_i32p, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
+    "belt_latent_decompress_varlen": [c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_i32, c_i32p, c_vp,
+                                      c_i32, c_i32p, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp,
+                                      c_vp],
+    "belt_prefill_attention_varlen": [c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_i32p, c_i32,
+                                      c_f32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp, c_vp],
+    "belt_attn_fold": [c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_i32, c_i32p, c_vp],
     "belt_prefill_attention": [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i64, c_i64, c_i32, c_i32, c_i32, c_f32,
                                c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_q_norm_rope": [c_vp, c_i32, c_i64, c_i64, c_vp, c_f32, c_vp, c_i32, c_i32, c_vp, c_i32, c_vp, c_i64, c_i64,

@@ -605,53 +605,62 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
 }
 
-int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
-                           int64_t stride_block, int64_t stride_tok, const int32_t* block_table_row, int32_t seq_len,
-                           int32_t pos0, int32_t count, const void* wk, int32_t kc, const int32_t* k_segs,
-                           const void* v_up, int32_t v_offset, int32_t r_v, const void* cos_sin, int32_t max_pos,
-                           void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The piece list of a varlen decompress: host [n][4] = (request row of block_table, seq_len, pos0, count); outputs
+// concatenated in piece order. Runs ceil(n / kVarlenMax) launches.
+int decompress_pieces(const char* who, const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                      int64_t stride_block, int64_t stride_tok, const int32_t* block_table, int64_t bt_stride,
+                      int32_t num_pieces, const int32_t* pieces, const void* wk, int32_t kc, const int32_t* k_segs,
+                      const void* v_up, int32_t v_offset, int32_t r_v, const void* cos_sin, int32_t max_pos,
+                      void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, cudaStream_t stream) {
   using namespace belt;
-  if (count < 0 || pos0 < 0 || seq_len < 0 || static_cast<int64_t>(pos0) + count > seq_len)
-    return fail(BELT_ERR_INVALID, "latent_decompress: positions [%d, %d) outside the request's %d", pos0, pos0 + count,
-                seq_len);
-  if (count == 0) return ok();
-  if (!cache || !block_table_row || !wk || !k_segs || !v_up || !cos_sin || !k_out || !v_out)
-    return fail(BELT_ERR_INVALID, "latent_decompress: null buffer");
+  if (num_pieces < 0 || (num_pieces > 0 && !pieces)) return fail(BELT_ERR_INVALID, "%s: piece list", who);
+  long long total = 0;
+  for (int i = 0; i < num_pieces; ++i) {
+    const int req = pieces[4 * i], seq_len = pieces[4 * i + 1], pos0 = pieces[4 * i + 2], count = pieces[4 * i + 3];
+    if (req < 0 || count < 0 || pos0 < 0 || seq_len < 0 || static_cast<int64_t>(pos0) + count > seq_len)
+      return fail(BELT_ERR_INVALID, "%s: piece %d: positions [%d, %d) outside the request's %d (request %d)", who, i,
+                  pos0, pos0 + count, seq_len, req);
+    if (seq_len > max_pos)
+      return fail(BELT_ERR_INVALID, "%s: cos_sin has %d rows < %d", who, max_pos, seq_len);
+    total += count;
+  }
+  if (total == 0) return ok();
+  if (!cache || !block_table || !wk || !k_segs || !v_up || !cos_sin || !k_out || !v_out)
+    return fail(BELT_ERR_INVALID, "%s: null buffer", who);
   if (!(page == 16 || page == 32 || page == 64 || (page % 128 == 0 && page > 0)))
-    return fail(BELT_ERR_INVALID, "latent_decompress: page size %d (supported: 16, 32, 64 or a multiple of 128)", page);
+    return fail(BELT_ERR_INVALID, "%s: page size %d (supported: 16, 32, 64 or a multiple of 128)", who, page);
   if (num_blocks < 1 || num_blocks > (1ll << 31) - 2 || row_width <= 0 || stride_tok < row_width || stride_tok % 8 ||
       stride_block % 8 || !aligned16(cache))
-    return fail(BELT_ERR_INVALID, "latent_decompress: cache rows must be 16-byte aligned (strides %lld, %lld)",
+    return fail(BELT_ERR_INVALID, "%s: cache rows must be 16-byte aligned (strides %lld, %lld)", who,
                 (long long)stride_block, (long long)stride_tok);
   if (kc <= 0 || kc % 64 || kc > row_width + 63 || r_v <= 0 || r_v > 1024 || v_offset < 0 || v_offset + r_v > row_width)
-    return fail(BELT_ERR_INVALID, "latent_decompress: kc %d, v_offset %d, r_v %d, row width %d", kc, v_offset, r_v,
-                row_width);
-  if (max_pos < seq_len) return fail(BELT_ERR_INVALID, "latent_decompress: cos_sin has %d rows < %d", max_pos, seq_len);
+    return fail(BELT_ERR_INVALID, "%s: kc %d, v_offset %d, r_v %d, row width %d", who, kc, v_offset, r_v, row_width);
   if (!aligned16(wk) || !aligned16(v_up) || !aligned16(k_out) || !aligned16(v_out) || out_st % 8 || out_sg % 8 ||
       out_sg < 256 || out_st < 4 * out_sg)
-    return fail(BELT_ERR_INVALID, "latent_decompress: weights and outputs 16-byte aligned, output strides");
+    return fail(BELT_ERR_INVALID, "%s: weights and outputs 16-byte aligned, output strides", who);
   DecompressParams p{};
-  p.block_table = block_table_row;
-  p.seq_len = seq_len;
+  p.block_table = block_table;
+  p.bt_stride = bt_stride;
   p.page = page;
   p.num_blocks = static_cast<int>(num_blocks);
-  p.pos0 = pos0;
-  p.count = count;
   for (int g = 0; g < kG; ++g) {
     const int runs[2][2] = {{k_segs[4 * g], k_segs[4 * g + 1]}, {k_segs[4 * g + 2], k_segs[4 * g + 3]}};
     bool use[64] = {};
     for (int q = 0; q < 2; ++q) {
       if (runs[q][1] <= 0) continue;
       if (runs[q][0] < 0 || runs[q][0] + runs[q][1] > kc)
-        return fail(BELT_ERR_INVALID, "latent_decompress: k_segs of group %d outside the key part", g);
+        return fail(BELT_ERR_INVALID, "%s: k_segs of group %d outside the key part", who, g);
       for (int c = runs[q][0] >> 6; c <= (runs[q][0] + runs[q][1] - 1) >> 6 && c < 64; ++c) use[c] = true;
     }
     int n = 0;
     for (int c = 0; c < 64; ++c)
       if (use[c]) {
         if (n == kPwMaxChunks)
-          return fail(BELT_ERR_INVALID, "latent_decompress: group %d spans more than %d 64-column chunks", g,
-                      kPwMaxChunks);
+          return fail(BELT_ERR_INVALID, "%s: group %d spans more than %d 64-column chunks", who, g, kPwMaxChunks);
         p.k_chunk[g][n++] = c;
       }
     p.k_nch[g] = n;
@@ -689,59 +698,194 @@ int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, 
     int r = encode_bf16(&maps.v, v_up, 3, dims, strides, box, "v_up");
     if (r != BELT_OK) return r;
   }
-  cudaError_t e = launch_decompress(maps, p, as_stream(stream));
-  return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decompress launch");
+  long long row = 0;
+  for (int i0 = 0; i0 < num_pieces; i0 += kVarlenMax) {
+    const int n = num_pieces - i0 < kVarlenMax ? num_pieces - i0 : kVarlenMax;
+    p.num_pieces = n;
+    p.piece_cta0[0] = 0;
+    for (int i = 0; i < n; ++i) {
+      const int* pc = pieces + 4 * (i0 + i);
+      p.piece_req[i] = pc[0];
+      p.piece_len[i] = pc[1];
+      p.piece_pos0[i] = pc[2];
+      p.piece_count[i] = pc[3];
+      p.piece_out[i] = row;
+      row += pc[3];
+      p.piece_cta0[i + 1] = p.piece_cta0[i] + decompress_piece_ctas(pc[2], pc[3]);
+    }
+    cudaError_t e = launch_decompress(maps, p, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "latent_decompress launch");
+  }
+  return ok();
+}
+
+// The piece list of a varlen prefill attention: host [n][8] = (q_row, ql, k_row, S, q_pos0, k_pos0, o_row, to2).
+int prefill_pieces(const char* who, const void* q, int64_t q_rows, int64_t q_st, int64_t q_sh, const void* k,
+                   const void* v, int64_t k_rows, int64_t kv_st, int64_t kv_sg, int32_t num_pieces,
+                   const int32_t* pieces, int32_t causal, float scale, void* out, void* out2, int64_t out_st,
+                   int64_t out_sh, float* lse, float* lse2, int64_t lse_st, int32_t* err, cudaStream_t stream) {
+  using namespace belt;
+  if (num_pieces < 0 || (num_pieces > 0 && !pieces) || q_rows < 0 || k_rows < 0)
+    return fail(BELT_ERR_INVALID, "%s: piece list", who);
+  long long tiles = 0;
+  bool any_keys = false;
+  for (int i = 0; i < num_pieces; ++i) {
+    const int* pc = pieces + 8 * i;
+    if (pc[1] < 0 || pc[3] < 0 || pc[0] < 0 || pc[2] < 0 || pc[6] < 0 || pc[0] + static_cast<int64_t>(pc[1]) > q_rows ||
+        pc[2] + static_cast<int64_t>(pc[3]) > k_rows)
+      return fail(BELT_ERR_INVALID, "%s: piece %d: query rows [%d, +%d) of %lld, key rows [%d, +%d) of %lld", who, i,
+                  pc[0], pc[1], (long long)q_rows, pc[2], pc[3], (long long)k_rows);
+    if (pc[7] && !out2) return fail(BELT_ERR_INVALID, "%s: piece %d writes to out2, which is null", who, i);
+    tiles += (pc[1] + 127) / 128;
+    any_keys = any_keys || pc[3] > 0;
+  }
+  if (tiles == 0) return ok();
+  if (!q || !out || (any_keys && (!k || !v))) return fail(BELT_ERR_INVALID, "%s: null buffer", who);
+  if (!aligned16(q) || !aligned16(out) || (out2 && !aligned16(out2)) || (any_keys && (!aligned16(k) || !aligned16(v))) ||
+      q_st % 8 || q_sh % 8 || kv_st % 8 || kv_sg % 8 || out_st % 8 || out_sh % 8 || q_sh < 256 || q_st < kH * q_sh ||
+      kv_sg < 256 || kv_st < kG * kv_sg || out_sh < 256 || out_st < kH * out_sh)
+    return fail(BELT_ERR_INVALID, "%s: 16-byte aligned tensors, strides multiples of 8 elements", who);
+  if ((lse || lse2) && lse_st < kH) return fail(BELT_ERR_INVALID, "%s: lse row stride %lld", who, (long long)lse_st);
+  PrefillAttnParams p{};
+  p.H = kH;
+  p.hpg = kHPG;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out2 = static_cast<__nv_bfloat16*>(out2);
+  p.out_st = out_st;
+  p.out_sh = out_sh;
+  p.lse = lse;
+  p.lse2 = lse2;
+  p.lse_st = lse_st;
+  p.err = err;
+  PrefillAttnMaps maps;
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kH), static_cast<cuuint64_t>(q_rows)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(q_sh) * 2, static_cast<cuuint64_t>(q_st) * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    int r = encode_bf16(&maps.q, q, 3, dims, strides, box, "q");
+    if (r != BELT_OK) return r;
+  }
+  const long long nk = k_rows > 0 ? k_rows : 1;   // a map of one row when there are no keys (never read)
+  {
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kG), static_cast<cuuint64_t>(nk)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kv_sg) * 2, static_cast<cuuint64_t>(kv_st) * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    int r = encode_bf16(&maps.k, any_keys ? k : q, 3, dims, strides, box, "k");
+    if (r != BELT_OK) return r;
+    r = encode_bf16(&maps.v, any_keys ? v : q, 3, dims, strides, box, "v");
+    if (r != BELT_OK) return r;
+  }
+  for (int i0 = 0; i0 < num_pieces; i0 += kVarlenMax) {
+    const int n = num_pieces - i0 < kVarlenMax ? num_pieces - i0 : kVarlenMax;
+    p.num_pieces = n;
+    p.piece_cta0[0] = 0;
+    for (int i = 0; i < n; ++i) {
+      const int* pc = pieces + 8 * (i0 + i);
+      p.piece_q_row[i] = pc[0];
+      p.piece_ql[i] = pc[1];
+      p.piece_k_row[i] = pc[2];
+      p.piece_S[i] = pc[3];
+      p.piece_q_pos0[i] = pc[4];
+      p.piece_k_pos0[i] = pc[5];
+      p.piece_o_row[i] = pc[6];
+      p.piece_to2[i] = pc[7];
+      p.piece_cta0[i + 1] = p.piece_cta0[i] + (pc[1] + 127) / 128;
+    }
+    cudaError_t e = launch_prefill_attn(maps, p, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill_attention launch");
+  }
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int belt_latent_decompress(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                           int64_t stride_block, int64_t stride_tok, const int32_t* block_table_row, int32_t seq_len,
+                           int32_t pos0, int32_t count, const void* wk, int32_t kc, const int32_t* k_segs,
+                           const void* v_up, int32_t v_offset, int32_t r_v, const void* cos_sin, int32_t max_pos,
+                           void* k_out, void* v_out, int64_t out_st, int64_t out_sg, int32_t* err, void* stream) {
+  const int32_t piece[4] = {0, seq_len, pos0, count};
+  return decompress_pieces("latent_decompress", cache, num_blocks, page, row_width, stride_block, stride_tok,
+                           block_table_row, 0, 1, piece, wk, kc, k_segs, v_up, v_offset, r_v, cos_sin, max_pos, k_out,
+                           v_out, out_st, out_sg, err, as_stream(stream));
+}
+
+int belt_latent_decompress_varlen(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                                  int64_t stride_block, int64_t stride_tok, const int32_t* block_table,
+                                  int64_t bt_stride, int32_t num_pieces, const int32_t* pieces, const void* wk,
+                                  int32_t kc, const int32_t* k_segs, const void* v_up, int32_t v_offset, int32_t r_v,
+                                  const void* cos_sin, int32_t max_pos, void* k_out, void* v_out, int64_t out_st,
+                                  int64_t out_sg, int32_t* err, void* stream) {
+  return decompress_pieces("latent_decompress_varlen", cache, num_blocks, page, row_width, stride_block, stride_tok,
+                           block_table, bt_stride, num_pieces, pieces, wk, kc, k_segs, v_up, v_offset, r_v, cos_sin,
+                           max_pos, k_out, v_out, out_st, out_sg, err, as_stream(stream));
 }
 
 int belt_prefill_attention(const void* q, int32_t ql, int64_t q_st, int64_t q_sh, const void* k, const void* v,
                            int32_t num_keys, int64_t kv_st, int64_t kv_sg, int32_t q_pos0, int32_t k_pos0,
                            int32_t causal, float scale, void* out, int64_t out_st, int64_t out_sh, float* lse,
                            int64_t lse_st, int32_t* err, void* stream) {
-  using namespace belt;
   if (ql < 0 || num_keys < 0) return fail(BELT_ERR_INVALID, "prefill_attention: ql %d, keys %d", ql, num_keys);
-  if (ql == 0) return ok();
-  if (!q || !out || (num_keys > 0 && (!k || !v)))
-    return fail(BELT_ERR_INVALID, "prefill_attention: null buffer");
-  if (!aligned16(q) || !aligned16(out) || (num_keys > 0 && (!aligned16(k) || !aligned16(v))) || q_st % 8 ||
-      q_sh % 8 || kv_st % 8 || kv_sg % 8 || out_st % 8 || out_sh % 8 || q_sh < 256 || q_st < kH * q_sh ||
-      kv_sg < 256 || kv_st < kG * kv_sg || out_sh < 256 || out_st < kH * out_sh)
-    return fail(BELT_ERR_INVALID, "prefill_attention: 16-byte aligned tensors, strides multiples of 8 elements");
-  if (lse && lse_st < kH) return fail(BELT_ERR_INVALID, "prefill_attention: lse row stride %lld", (long long)lse_st);
-  PrefillAttnParams p{};
-  p.ql = ql;
-  p.S = num_keys;
-  p.H = kH;
-  p.hpg = kHPG;
-  p.q_pos0 = q_pos0;
-  p.k_pos0 = k_pos0;
-  p.causal = causal ? 1 : 0;
-  p.scale_log2 = scale * 1.4426950408889634f;
+  const int32_t piece[8] = {0, ql, 0, num_keys, q_pos0, k_pos0, 0, 0};
+  return prefill_pieces("prefill_attention", q, ql, q_st, q_sh, k, v, num_keys, kv_st, kv_sg, 1, piece, causal, scale,
+                        out, nullptr, out_st, out_sh, lse, nullptr, lse_st, err, as_stream(stream));
+}
+
+int belt_prefill_attention_varlen(const void* q, int64_t q_rows, int64_t q_st, int64_t q_sh, const void* k,
+                                  const void* v, int64_t k_rows, int64_t kv_st, int64_t kv_sg, int32_t num_pieces,
+                                  const int32_t* pieces, int32_t causal, float scale, void* out, void* out2,
+                                  int64_t out_st, int64_t out_sh, float* lse, float* lse2, int64_t lse_st,
+                                  int32_t* err, void* stream) {
+  return prefill_pieces("prefill_attention_varlen", q, q_rows, q_st, q_sh, k, v, k_rows, kv_st, kv_sg, num_pieces,
+                        pieces, causal, scale, out, out2, out_st, out_sh, lse, lse2, lse_st, err, as_stream(stream));
+}
+
+int belt_attn_fold(void* out, int64_t out_st, int64_t out_sh, float* lse, int64_t lse_st, const void* part,
+                   int64_t part_st, int64_t part_sh, const float* part_lse, int64_t plse_st, int32_t num_pieces,
+                   const int32_t* pieces, void* stream) {
+  using namespace belt;
+  if (num_pieces < 0 || (num_pieces > 0 && !pieces)) return fail(BELT_ERR_INVALID, "attn_fold: piece list");
+  long long rows = 0;
+  for (int i = 0; i < num_pieces; ++i) {
+    if (pieces[3 * i] < 0 || pieces[3 * i + 1] < 0 || pieces[3 * i + 2] < 0)
+      return fail(BELT_ERR_INVALID, "attn_fold: piece %d", i);
+    rows += pieces[3 * i + 2];
+  }
+  if (rows == 0) return ok();
+  if (!out || !lse || !part || !part_lse) return fail(BELT_ERR_INVALID, "attn_fold: null buffer");
+  if (!aligned16(out) || !aligned16(part) || out_st % 8 || out_sh % 8 || part_st % 8 || part_sh % 8 || out_sh < 256 ||
+      part_sh < 256 || lse_st < kH || plse_st < kH)
+    return fail(BELT_ERR_INVALID, "attn_fold: 16-byte aligned rows, strides multiples of 8 elements");
+  AttnFoldParams p{};
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_st = out_st;
   p.out_sh = out_sh;
   p.lse = lse;
   p.lse_st = lse_st;
-  p.err = err;
-  PrefillAttnMaps maps;
-  {
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kH), static_cast<cuuint64_t>(ql)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(q_sh) * 2, static_cast<cuuint64_t>(q_st) * 2};
-    cuuint32_t box[3] = {64, 1, 128};
-    int r = encode_bf16(&maps.q, q, 3, dims, strides, box, "q");
-    if (r != BELT_OK) return r;
+  p.part = static_cast<const __nv_bfloat16*>(part);
+  p.part_st = part_st;
+  p.part_sh = part_sh;
+  p.plse = part_lse;
+  p.plse_st = plse_st;
+  p.H = kH;
+  for (int i0 = 0; i0 < num_pieces; i0 += kVarlenMax) {
+    const int n = num_pieces - i0 < kVarlenMax ? num_pieces - i0 : kVarlenMax;
+    p.num_pieces = n;
+    p.piece_row0[0] = 0;
+    for (int i = 0; i < n; ++i) {
+      p.piece_dst[i] = pieces[3 * (i0 + i)];
+      p.piece_src[i] = pieces[3 * (i0 + i) + 1];
+      p.piece_rows[i] = pieces[3 * (i0 + i) + 2];
+      p.piece_row0[i + 1] = p.piece_row0[i] + p.piece_rows[i];
+    }
+    cudaError_t e = launch_attn_fold(p, as_stream(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "attn_fold launch");
   }
-  const int nk = num_keys > 0 ? num_keys : 1;   // a map of one row when there are no keys (never read)
-  {
-    cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kG), static_cast<cuuint64_t>(nk)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(kv_sg) * 2, static_cast<cuuint64_t>(kv_st) * 2};
-    cuuint32_t box[3] = {64, 1, 128};
-    int r = encode_bf16(&maps.k, num_keys > 0 ? k : q, 3, dims, strides, box, "k");
-    if (r != BELT_OK) return r;
-    r = encode_bf16(&maps.v, num_keys > 0 ? v : q, 3, dims, strides, box, "v");
-    if (r != BELT_OK) return r;
-  }
-  cudaError_t e = launch_prefill_attn(maps, p, as_stream(stream));
-  return e == cudaSuccess ? ok() : cuda_fail(e, "prefill_attention launch");
+  return ok();
 }
 
 int belt_q_norm_rope(const void* qg, int32_t num_tokens, int64_t qg_st, int64_t qg_sh, const float* norm_weight,

@@ -7,8 +7,11 @@
 //     v      = bf16(rows[:, v_off : v_off + r_v] . v_up[g]) [S, 256]
 //     k[s, g] = [k_pe | k_nope], v[s, g]                    BF16 outputs [count, 4, 256]
 //
-// One CTA (128 threads) per (two 128-position tiles, group, part): part 0 the group's keys (N = 256 = 64 rope + 192 nope
-// rows of wk[g] = [rope_up[g]; qmap[g, 64:]], K = the group's column window, at most five 64-column chunks), part 1
+// Varlen: one launch covers several pieces (a request's positions [pos0, pos0 + count) each, its rows through its own
+// block-table row), the outputs of piece i from row piece_out[i]; the CTAs of a piece are consecutive along x.
+// One CTA (128 threads) per (two 128-position tiles of a piece, group, part): part 0 the group's keys (N = 256 = 64
+// rope + 192 nope rows of wk[g] = [rope_up[g]; qmap[g, 64:]], K = the group's column window, at most five 64-column
+// chunks), part 1
 // its values (N = 256, K = the value columns). Tiles sit at absolute positions (multiples of 128), so every page box
 // covers whole rows of one page; rows outside [pos0, pos0 + count) are computed and dropped. The two tiles of a CTA
 // share every weight chunk (two MMAs per K step into two TMEM accumulators): the weights stream once per 256 positions.
@@ -44,7 +47,12 @@ __global__ void __launch_bounds__(kDcThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
-  const int tile_pos = (p.pos0 / 128 + kDcTiles * static_cast<int>(blockIdx.x)) * 128;   // row 0 of tile 0
+  int pi = 0;   // this CTA's piece
+  while (pi + 1 < p.num_pieces && static_cast<int>(blockIdx.x) >= p.piece_cta0[pi + 1]) ++pi;
+  const int seq_len = p.piece_len[pi], pos0 = p.piece_pos0[pi], count = p.piece_count[pi];
+  const int32_t* block_table = p.block_table + static_cast<long long>(p.piece_req[pi]) * p.bt_stride;
+  const long long out_row0 = p.piece_out[pi];
+  const int tile_pos = (pos0 / 128 + kDcTiles * (static_cast<int>(blockIdx.x) - p.piece_cta0[pi])) * 128;
   const int g = blockIdx.y;
   const bool values = blockIdx.z != 0;
   const int nchunks = values ? p.v_nch : p.k_nch[g];
@@ -68,12 +76,12 @@ __global__ void __launch_bounds__(kDcThreads, 1)
     // ---------------------------------------------------------------- producer
     // the tile's page boxes: block id and first row of every box (positions past the request read as zeros)
     int blk[kDcTiles][8], row0[kDcTiles][8];
-    const int npages = (p.seq_len + p.page - 1) / p.page;
+    const int npages = (seq_len + p.page - 1) / p.page;
     for (int t = 0; t < kDcTiles; ++t)
       for (int b = 0; b < n_boxes; ++b) {
         const int pos = tile_pos + 128 * t + b * box_rows;
         const int pg = pos / p.page;
-        blk[t][b] = pg < npages ? __ldg(p.block_table + pg) : p.num_blocks;
+        blk[t][b] = pg < npages ? __ldg(block_table + pg) : p.num_blocks;
         row0[t][b] = pos - pg * p.page;
       }
     int issued = 0;
@@ -142,16 +150,16 @@ __global__ void __launch_bounds__(kDcThreads, 1)
   for (int t = 0; t < kDcTiles; ++t) {
     if (done && !*abort_flag && nchunks == 0) {   // a group without columns: zero keys / values
       const int pos = tile_pos + 128 * t + threadIdx.x;
-      if (pos >= p.pos0 && pos < p.pos0 + p.count) {
-        uint4* dst = reinterpret_cast<uint4*>((values ? p.v_out : p.k_out) + static_cast<long long>(pos - p.pos0) * p.out_st +
+      if (pos >= pos0 && pos < pos0 + count) {
+        uint4* dst = reinterpret_cast<uint4*>((values ? p.v_out : p.k_out) + (out_row0 + pos - pos0) * p.out_st +
                                               static_cast<long long>(g) * p.out_sg);
         for (int q = 0; q < 32; ++q) dst[q] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     if (done && !*abort_flag && nchunks > 0) {
       const int pos = tile_pos + 128 * t + threadIdx.x;
-      const bool keep = pos >= p.pos0 && pos < p.pos0 + p.count;
-      __nv_bfloat16* out = (values ? p.v_out : p.k_out) + static_cast<long long>(pos - p.pos0) * p.out_st +
+      const bool keep = pos >= pos0 && pos < pos0 + count;
+      __nv_bfloat16* out = (values ? p.v_out : p.k_out) + (out_row0 + pos - pos0) * p.out_st +
                            static_cast<long long>(g) * p.out_sg;
       const uint32_t taddr = tmem + 256 * t + (static_cast<uint32_t>(warp * 32) << 16);
       int c0 = 0;
@@ -214,13 +222,20 @@ __global__ void __launch_bounds__(kDcThreads, 1)
 
 int decompress_smem_bytes() { return 1024 + kDcStages * kDcStage + kDcBars * 8 + 16; }
 
+// CTAs (along x) of a piece of `count` positions from pos0: pairs of 128-position tiles at absolute multiples of 128.
+int decompress_piece_ctas(int pos0, int count) {
+  if (count <= 0) return 0;
+  const int first = pos0 / 128, last = (pos0 + count - 1) / 128;
+  return (last - first + kDcTiles) / kDcTiles;
+}
+
 cudaError_t launch_decompress(const DecompressMaps& maps, const DecompressParams& p, cudaStream_t stream) {
-  if (p.count == 0) return cudaSuccess;
+  const int total = p.piece_cta0[p.num_pieces];
+  if (total == 0) return cudaSuccess;
   const int smem = decompress_smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(decompress_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  const int first = p.pos0 / 128, last = (p.pos0 + p.count - 1) / 128;
-  dim3 grid((last - first + kDcTiles) / kDcTiles, kG, 2);
+  dim3 grid(total, kG, 2);
   decompress_kernel<<<grid, kDcThreads, smem, stream>>>(maps, p);
   return cudaGetLastError();
 }

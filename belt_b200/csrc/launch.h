@@ -190,10 +190,18 @@ struct DecompressMaps {
   CUtensorMap wk;      // [4, 256, kc] key weights, box {64, 256, 1}
   CUtensorMap v;       // v_up [4, r_v, 256], box {64, 64, 1}
 };
+// Varlen launches (decompress, prefill attention, fold) carry a table of up to kVarlenMax pieces in their parameters;
+// the C ABI splits longer lists into several launches.
+constexpr int kVarlenMax = 64;
 struct DecompressParams {
-  const int32_t* block_table;   // the request's row
-  int seq_len, page, num_blocks;
-  int pos0, count;
+  const int32_t* block_table;   // [requests, >= pages] int32, row stride bt_stride
+  long long bt_stride;
+  int page, num_blocks;
+  // pieces: positions [pos0, pos0 + count) of request `req` (seq_len cached tokens), written from row `out_row`
+  int num_pieces;
+  int piece_req[kVarlenMax], piece_len[kVarlenMax], piece_pos0[kVarlenMax], piece_count[kVarlenMax];
+  long long piece_out[kVarlenMax];
+  int piece_cta0[kVarlenMax + 1];   // first CTA (grid x) of every piece, and the total
   int k_nch[4];
   int k_chunk[4][kPwMaxChunks];
   int v_chunk0, v_nch, v_offset;
@@ -205,6 +213,7 @@ struct DecompressParams {
   int* err;
 };
 cudaError_t launch_decompress(const DecompressMaps& maps, const DecompressParams& p, cudaStream_t stream);
+int decompress_piece_ctas(int pos0, int count);
 
 // Prefill attention (prefill_attn.cu).
 struct PrefillAttnMaps {
@@ -213,16 +222,43 @@ struct PrefillAttnMaps {
   CUtensorMap v;
 };
 struct PrefillAttnParams {
-  int ql, S, H, hpg;
-  int q_pos0, k_pos0, causal;
+  int H, hpg, causal;
   float scale_log2;
+  // pieces: queries [q_row, q_row + ql) at positions q_pos0.. over keys [k_row, k_row + S) at positions k_pos0..;
+  // outputs (and LSEs) from row o_row of out / lse, or of out2 / lse2 when to2 is set
+  int num_pieces;
+  int piece_q_row[kVarlenMax], piece_ql[kVarlenMax], piece_k_row[kVarlenMax], piece_S[kVarlenMax];
+  int piece_q_pos0[kVarlenMax], piece_k_pos0[kVarlenMax], piece_o_row[kVarlenMax], piece_to2[kVarlenMax];
+  int piece_cta0[kVarlenMax + 1];   // first query tile (grid x) of every piece, and the total
   __nv_bfloat16* out;
+  __nv_bfloat16* out2;
   long long out_st, out_sh;
-  float* lse;          // [ql, H] (row stride lse_st), may be null
+  float* lse;          // [rows, H] (row stride lse_st), may be null
+  float* lse2;
   long long lse_st;
   int* err;
 };
 cudaError_t launch_prefill_attn(const PrefillAttnMaps& maps, const PrefillAttnParams& p, cudaStream_t stream);
+
+// Log-sum-exp fold of a chunk's attention result into a running one (attn_fold.cu), in place:
+//   out[dst] = bf16((out[dst] e^(lse[dst] - m) + part[src] e^(plse[src] - m)) / s), lse[dst] = m + log s
+// for the rows of every piece (dst_row.., src_row.., rows); a part row with LSE -inf leaves its row unchanged, an out row
+// with LSE -inf takes the part row.
+struct AttnFoldParams {
+  __nv_bfloat16* out;
+  long long out_st, out_sh;
+  float* lse;
+  long long lse_st;
+  const __nv_bfloat16* part;
+  long long part_st, part_sh;
+  const float* plse;
+  long long plse_st;
+  int H;
+  int num_pieces;
+  int piece_dst[kVarlenMax], piece_src[kVarlenMax], piece_rows[kVarlenMax];
+  int piece_row0[kVarlenMax + 1];   // first grid row of every piece, and the total
+};
+cudaError_t launch_attn_fold(const AttnFoldParams& p, cudaStream_t stream);
 
 // Element-wise steps around the attention (model_ops.cu).
 struct QNormRopeParams {

@@ -6,22 +6,23 @@
 //     out[b, h, :] = bf16( U_v,g(h) a[b, h, :] )                   (FP32 accumulation)
 // The roundings are the unfused path's (a rounded to BF16 before the projection), so the two agree to one BF16 ulp.
 //
-// One CTA per (head, tile of 32 requests), 128 threads:
+// One CTA per (head, tile of 32 requests), 1024 threads (a warp per request):
 //   * thread 0 streams U_v^T of the head's group ([r_v, 256], channels contiguous) in 64-deep K blocks, four boxes of
 //     64 channels x 64 k (MN-major, 128-byte swizzle) per stage, from the start (it does not depend on the merge);
-//   * all warps merge: warp w takes requests w, w + 4, ..; the lanes reduce the segment LSEs, then sweep the r_v
-//     features (coalesced rows of part) and write a as the K-major B operand (32 requests x r_v, 128-byte swizzle);
+//   * warp j merges request j: its lanes reduce the segment LSEs in one pass (a running max and sum per lane, then
+//     across the warp), then sweep the r_v features (coalesced rows of part, the rows of up to four segments in flight
+//     together) and write a as the K-major B operand (32 requests x r_v, 128-byte swizzle);
 //   * thread 32 issues tcgen05 out^T[channel, request] += U_v^T[channel, k] a^T[k, request]: M = 128 channels (two
 //     halves), N = 32 requests, K = 16 per instruction, into TMEM;
-//   * epilogue: thread (warp w, lane l) holds channel 32 w + l of both halves for the 32 requests; a warp's stores of
-//     one request cover 32 consecutive channels (64 bytes).
+//   * epilogue (warps 0-3): thread (warp w, lane l) holds channel 32 w + l of both halves for the 32 requests; a warp's
+//     stores of one request cover 32 consecutive channels (64 bytes).
 #include "common.cuh"
 #include "launch.h"
 
 namespace belt {
 
 namespace {
-constexpr int kMuThreads = 128;
+constexpr int kMuThreads = 1024;
 constexpr int kMuReqs = 32;                         // requests per CTA (the MMA's N)
 constexpr int kMuStageBytes = 4 * 64 * 128;         // 256 channels x 64 k x 2 B = 32 KB
 constexpr int kMuStages = 3;
@@ -29,8 +30,8 @@ constexpr int kMuMaxChunks = 10;                    // r_v <= 640
 constexpr int kMuBChunk = kMuReqs * 128;            // 32 requests x 64 k x 2 B = 4 KB per K block
 constexpr int kMuOffB = kMuStages * kMuStageBytes;  // 96 KB
 constexpr int kMuOffW = kMuOffB + kMuMaxChunks * kMuBChunk;   // per-warp segment weights
-constexpr int kMuWeights = 256;                     // segment weights staged per pass, per warp
-constexpr int kMuOffBars = kMuOffW + 4 * kMuWeights * 4;
+constexpr int kMuWeights = 64;                      // segment weights staged per pass, per warp (more than 32)
+constexpr int kMuOffBars = kMuOffW + (kMuThreads / 32) * kMuWeights * 4;
 // barriers: full[3], empty[3], done
 constexpr int uFull = 0, uEmpty = 3, uDone = 6, kMuBars = 7;
 
@@ -84,45 +85,76 @@ __global__ void __launch_bounds__(kMuThreads, 1)
     reinterpret_cast<uint4*>(sB)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
   float* wts = wts_all + warp * kMuWeights;
-  for (int j = warp; j < kMuReqs; j += 4) {
-    const int b = b0 + j;
-    if (b >= p.num_reqs) break;
-    const int s0 = __ldg(p.seg_base + b), n = __ldg(p.seg_base + b + 1) - s0;
-    const float* base = p.part + static_cast<long long>(s0) * p.ps + static_cast<long long>(h) * p.ph;
-    float m = -INFINITY;
-    for (int s = lane; s < n; s += 32) m = fmaxf(m, __ldg(base + static_cast<long long>(s) * p.ps + p.lv));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float den = 0.f;
-    for (int s = lane; s < n; s += 32) den += __expf(__ldg(base + static_cast<long long>(s) * p.ps + p.lv) - m);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    const bool has = den > 0.f;
-    const float inv = has ? 1.f / den : 0.f;
-    if (lane == 0 && p.lse) p.lse[static_cast<long long>(b) * p.slb + h] = has ? m + __logf(den) : -INFINITY;
-    for (int f0 = 0; f0 < p.lv; f0 += 32 * 8) {
-      float acc[8] = {};
-      for (int sw = 0; sw < n; sw += kMuWeights) {
-        const int cnt = min(kMuWeights, n - sw);
-        __syncwarp();
-        for (int i = lane; i < cnt; i += 32)
-          wts[i] = __expf(__ldg(base + static_cast<long long>(sw + i) * p.ps + p.lv) - m);
-        __syncwarp();
-        for (int i = 0; i < cnt; ++i) {
-          const float w = wts[i];
-          const float* row = base + static_cast<long long>(sw + i) * p.ps;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const int f = f0 + 32 * q + lane;
-            if (f < p.lv) acc[q] = fmaf(w, __ldg(row + f), acc[q]);
-          }
-        }
+  {
+    const int j = warp, b = b0 + warp;
+    if (b < p.num_reqs) {
+      const int s0 = __ldg(p.seg_base + b), n = __ldg(p.seg_base + b + 1) - s0;
+      const float* base = p.part + static_cast<long long>(s0) * p.ps + static_cast<long long>(h) * p.ph;
+      // the segment LSEs' max, then the sum of their exponentials (the order and arithmetic of belt_merge_segments,
+      // so that the merged output rounds the same way)
+      float m = -INFINITY, my_lse = -INFINITY;
+      for (int s = lane; s < n; s += 32) {
+        const float l = __ldg(base + static_cast<long long>(s) * p.ps + p.lv);
+        if (s == lane) my_lse = l;
+        m = fmaxf(m, l);
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int f = f0 + 32 * q + lane;
-        if (f < p.lv)
-          *reinterpret_cast<__nv_bfloat16*>(sB + sw128_elem(j, f, kMuReqs)) = __float2bfloat16_rn(acc[q] * inv);
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float d = 0.f;
+      for (int s = lane; s < n; s += 32)
+        d += __expf((s == lane ? my_lse : __ldg(base + static_cast<long long>(s) * p.ps + p.lv)) - m);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const bool has = d > 0.f;
+      const float inv = has ? 1.f / d : 0.f;
+      if (lane == 0 && p.lse) p.lse[static_cast<long long>(b) * p.slb + h] = has ? m + __logf(d) : -INFINITY;
+      const float my_w = lane < n ? __expf(my_lse - m) : 0.f;   // lane s < 32: the weight of segment s
+      for (int f0 = 0; f0 < p.lv; f0 += 32 * 8) {
+        float acc[8] = {};
+        if (n <= 32) {
+          // segment weights from the lanes that loaded them; four segments' rows in flight together
+          for (int s4 = 0; s4 < n; s4 += 4) {
+            float v[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float* row = base + static_cast<long long>(s4 + u) * p.ps;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int f = f0 + 32 * q + lane;
+                v[u][q] = (s4 + u < n && f < p.lv) ? __ldg(row + f) : 0.f;
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float w = __shfl_sync(0xffffffffu, my_w, (s4 + u) & 31);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc[q] = fmaf(s4 + u < n ? w : 0.f, v[u][q], acc[q]);
+            }
+          }
+        } else {
+          for (int sw = 0; sw < n; sw += kMuWeights) {
+            const int cnt = min(kMuWeights, n - sw);
+            __syncwarp();
+            for (int i = lane; i < cnt; i += 32)
+              wts[i] = __expf(__ldg(base + static_cast<long long>(sw + i) * p.ps + p.lv) - m);
+            __syncwarp();
+            for (int i = 0; i < cnt; ++i) {
+              const float w = wts[i];
+              const float* row = base + static_cast<long long>(sw + i) * p.ps;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int f = f0 + 32 * q + lane;
+                if (f < p.lv) acc[q] = fmaf(w, __ldg(row + f), acc[q]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int f = f0 + 32 * q + lane;
+          if (f < p.lv)
+            *reinterpret_cast<__nv_bfloat16*>(sB + sw128_elem(j, f, kMuReqs)) = __float2bfloat16_rn(acc[q] * inv);
+        }
       }
     }
   }
@@ -169,7 +201,8 @@ __global__ void __launch_bounds__(kMuThreads, 1)
   __syncwarp();
 
   // ---------------------------------------------------------------- epilogue
-  const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(&bars[uDone], 0, p.err, kErrTimeoutEpilogue));
+  const bool done =
+      warp < 4 && __all_sync(0xffffffffu, mbar_wait_bounded(&bars[uDone], 0, p.err, kErrTimeoutEpilogue));
   tc_fence_after();
   if (done && !*abort_flag) {
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;

@@ -4,7 +4,10 @@
 // their group's keys (24 query heads, 4 groups, head dim 256), causal by position, with the natural-log LSE of every
 // (query, head) so that the backend can fold context chunks together.
 //
-// One CTA per (128-query tile, head), 224 threads:
+// Varlen: one launch covers several pieces, each the queries of one request over a range of its keys (rows of the
+// concatenated query and key / value buffers, at their own positions), its output and LSE rows in `out` / `lse` or in
+// `out2` / `lse2`; the query tiles of a piece are consecutive along grid x.
+// One CTA per (128-query tile of a piece, head), 224 threads:
 //   * warp 0, lane 0: TMA producer of the query tile (128 x 256, K-major, 4 chunks of 64 columns, 128-byte swizzle)
 //     once and of the key tiles (same layout), warp 6, lane 0: producer of the value tiles (read as the MN-major B
 //     operand: 128 key rows of 64 channels per chunk). Each buffer holds one tile; the key buffer is refilled chunk
@@ -52,12 +55,16 @@ __global__ void __launch_bounds__(kPaThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int i0 = blockIdx.x * kPaTile, h = blockIdx.y, g = h / p.hpg;
-  const int q_last = min(i0 + kPaTile, p.ql) - 1;   // last live query of the tile
+  int pi = 0;   // this CTA's piece
+  while (pi + 1 < p.num_pieces && static_cast<int>(blockIdx.x) >= p.piece_cta0[pi + 1]) ++pi;
+  const int ql = p.piece_ql[pi], S = p.piece_S[pi], q_pos0 = p.piece_q_pos0[pi], k_pos0 = p.piece_k_pos0[pi];
+  const int q_row = p.piece_q_row[pi], k_row = p.piece_k_row[pi];
+  const int i0 = (static_cast<int>(blockIdx.x) - p.piece_cta0[pi]) * kPaTile, h = blockIdx.y, g = h / p.hpg;
+  const int q_last = min(i0 + kPaTile, ql) - 1;   // last live query of the tile
   // key tiles to visit: all of them, or causally those holding a key at or before the tile's last query position
-  int n_tiles = (p.S + kPaTile - 1) / kPaTile;
+  int n_tiles = (S + kPaTile - 1) / kPaTile;
   if (p.causal) {
-    const long long last_key = static_cast<long long>(p.q_pos0) + q_last - p.k_pos0;   // last key index allowed
+    const long long last_key = static_cast<long long>(q_pos0) + q_last - k_pos0;   // last key index allowed
     const long long lim = last_key < 0 ? 0 : last_key / kPaTile + 1;
     n_tiles = static_cast<int>(lim < n_tiles ? lim : n_tiles);
   }
@@ -90,7 +97,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
         mbar_arrive_expect_tx(&bars[full0 + c], per * kPaChunk);
         for (int q = 0; q < per; ++q)
           tma_load_3d(smem + off + (c * per + q) * kPaChunk, map, &bars[full0 + c], 64 * (c * per + q), g,
-                      j * kPaTile);
+                      k_row + j * kPaTile);
         ++issued[c];
       }
     if (*abort_flag)   // the latest copy into every chunk lands before the CTA's shared memory goes away
@@ -102,7 +109,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
     if (lane == 0 && n_tiles > 0) {
       mbar_arrive_expect_tx(&bars[aQ], kPaTileBytes);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tma_load_3d(smem + kPaQ + c * kPaChunk, &maps.q, &bars[aQ], 64 * c, h, i0);
+      for (int c = 0; c < 4; ++c) tma_load_3d(smem + kPaQ + c * kPaChunk, &maps.q, &bars[aQ], 64 * c, h, q_row + i0);
       stream_chunks(&maps.k, kPaK, aKFull, aKEmpty, 4, kErrTimeoutProducer);
       if (*abort_flag) mbar_wait_bounded(&bars[aQ], 0, nullptr, 0, kWaitCycles / 8);
     }
@@ -168,8 +175,8 @@ __global__ void __launch_bounds__(kPaThreads, 1)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const int qi = i0 + row;
-    const bool live_row = qi < p.ql;
-    const long long qpos = static_cast<long long>(p.q_pos0) + qi;
+    const bool live_row = qi < ql;
+    const long long qpos = static_cast<long long>(q_pos0) + qi;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
@@ -196,9 +203,9 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       if (lane == 0) mbar_arrive(&bars[aSFree]);
       // keys of this tile the row sees: all (no mask work), none, or a prefix (causal diagonal, the last tile)
       const int k0 = j * kPaTile;
-      long long kv = p.S - k0;
+      long long kv = S - k0;
       if (p.causal) {
-        const long long lim = qpos - p.k_pos0 - k0 + 1;
+        const long long lim = qpos - k_pos0 - k0 + 1;
         kv = lim < kv ? lim : kv;
       }
       const int nvis = !live_row ? 0 : kv <= 0 ? 0 : kv >= kPaTile ? kPaTile : static_cast<int>(kv);
@@ -263,7 +270,10 @@ __global__ void __launch_bounds__(kPaThreads, 1)
     tc_fence_after();
     if (ok && !*abort_flag) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* out = p.out + static_cast<long long>(qi) * p.out_st + static_cast<long long>(h) * p.out_sh;
+      const bool to2 = p.piece_to2[pi] != 0;
+      const long long orow = static_cast<long long>(p.piece_o_row[pi]) + qi;
+      __nv_bfloat16* out = (to2 ? p.out2 : p.out) + orow * p.out_st + static_cast<long long>(h) * p.out_sh;
+      float* lse_out = to2 ? p.lse2 : p.lse;
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint32_t o[32];
@@ -283,8 +293,8 @@ __global__ void __launch_bounds__(kPaThreads, 1)
                               pack_bf16(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
                               pack_bf16(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
       }
-      if (live_row && p.lse)
-        p.lse[static_cast<long long>(qi) * p.lse_st + h] =
+      if (live_row && lse_out)
+        lse_out[orow * p.lse_st + h] =
             l_run > 0.f ? (m_run + __log2f(l_run)) * 0.69314718055994530942f : -INFINITY;
     }
   }
@@ -300,11 +310,12 @@ __global__ void __launch_bounds__(kPaThreads, 1)
 int prefill_attn_smem_bytes() { return 1024 + kPaSmem + kPaBars * 8 + 16; }
 
 cudaError_t launch_prefill_attn(const PrefillAttnMaps& maps, const PrefillAttnParams& p, cudaStream_t stream) {
-  if (p.ql == 0) return cudaSuccess;
+  const int total = p.piece_cta0[p.num_pieces];
+  if (total == 0) return cudaSuccess;
   const int smem = prefill_attn_smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.ql + kPaTile - 1) / kPaTile, p.H);
+  dim3 grid(total, p.H);
   prefill_attn_kernel<<<grid, kPaThreads, smem, stream>>>(maps, p);
   return cudaGetLastError();
 }

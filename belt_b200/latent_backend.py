@@ -12,9 +12,10 @@ more, joined before the decode reads the cache), then:
 * decode (one query token per request, at the front of the batch): the block-diagonal query, the split-KV decode
   kernel over the paged rows on the step's schedule (computed once per step by the builder and shared by all layers),
   the merge of each request's segments and the per-head V up-projection written straight into ``output``;
-* prefill (everything else): keys and values rebuilt from the rows gathered through the block table in one tcgen05
-  kernel (``LatentLayer.decompress_paged``), causal attention on the tensor cores (``latent_ops.prefill_attention``),
-  chunked with a log-sum-exp merge beyond ``PREFILL_CHUNK`` context tokens.
+* prefill (everything else): for all prefill requests of the step together, keys and values rebuilt from the rows
+  gathered through the block table in one tcgen05 launch (``LatentLayer.decompress_varlen``) and causal attention on
+  the tensor cores in one more (``latent_ops.prefill_attention_varlen``), in rounds of at most ``PREFILL_CHUNK``
+  context tokens whose results are folded by log-sum-exp (``latent_ops.attn_fold``).
 
 When the running vLLM provides the plugin API the reference targets (``vllm_plugin.vllm_api``), the backend, the KV
 spec and the attention-type / block-size types are vLLM's own classes (``LatentAttentionBackend`` subclasses vLLM's
@@ -314,36 +315,57 @@ class LatentAttentionImpl:
 
     def _prefill(self, lat: LatentLayer, query: torch.Tensor, output: torch.Tensor, cache: torch.Tensor,
                  m: LatentAttentionMetadata) -> None:
-        """Each prefill request's new tokens over its whole context, causal (latent_backend.py:285-320): keys and values
-        rebuilt from the cache rows on the tensor cores (``LatentLayer.decompress_paged``) in chunks of
-        ``PREFILL_CHUNK`` context tokens, the tcgen05 attention kernel over each chunk (``latent_ops.
-        prefill_attention``), chunks folded by log-sum-exp (the reference's ``merge_attn_states``)."""
-        nd = m.num_decodes
-        tok = m.num_decode_tokens
-        for i in range(m.num_prefills):
-            b = nd + i
-            ql, L = m.prefill_q_len[i], m.prefill_seq_len[i]
-            q, dst = query[tok:tok + ql], output[tok:tok + ql]
-            step = PREFILL_CHUNK if PREFILL_CHUNK > 0 else L
-            if L <= step:
-                k, v = lat.decompress_paged(cache, m.block_table[b], L, 0, L)
-                latent_ops.prefill_attention(q, k, v, L - ql, 0, self.scale, causal=True, out=dst)
-            else:
-                acc, lse = None, None
-                for c0 in range(0, L, step):
-                    c1 = min(L, c0 + step)
-                    k, v = lat.decompress_paged(cache, m.block_table[b], L, c0, c1 - c0)
-                    o_c, l_c = latent_ops.prefill_attention(q, k, v, L - ql, c0, self.scale, causal=True)
-                    if acc is None:
-                        acc, lse = o_c.float(), l_c
-                        continue
-                    new = torch.logaddexp(lse, l_c)
-                    w_old = torch.exp(lse - new).nan_to_num(0.0)
-                    w_new = torch.exp(l_c - new).nan_to_num(0.0)
-                    acc = acc * w_old[..., None] + o_c.float() * w_new[..., None]
-                    lse = new
-                dst.copy_(acc.to(dst.dtype))
-            tok += ql
+        """Every prefill request's new tokens over its whole context, causal (latent_backend.py:285-320), all requests
+        of the step together: per round of at most ``PREFILL_CHUNK`` context tokens (``plan_prefill_rounds``), one
+        launch rebuilds the round's keys and values from the cache rows on the tensor cores
+        (``latent_ops.decompress_varlen``) and one runs the attention of every request over its part of them
+        (``latent_ops.prefill_attention_varlen``); the first part of a request writes its output rows directly, later
+        parts are folded into them by log-sum-exp (``latent_ops.attn_fold``, the reference's ``merge_attn_states``)."""
+        nd, tok0 = m.num_decodes, m.num_decode_tokens
+        qls, lens = m.prefill_q_len, m.prefill_seq_len
+        npt = sum(qls)
+        q_rel = [sum(qls[:i]) for i in range(len(qls))]       # rows of each request's tokens from tok0 on
+        q, out = query[tok0:tok0 + npt], output[tok0:tok0 + npt]
+        dev = query.device
+        lse = torch.empty(npt, self.num_heads, dtype=torch.float32, device=dev)
+        tmp = tmp_lse = None
+        for rnd in plan_prefill_rounds(lens, PREFILL_CHUNK):
+            k, v = lat.decompress_varlen(cache, m.block_table, [(nd + i, lens[i], k0, k1 - k0) for i, k0, k1 in rnd])
+            att, fold, krow = [], [], 0
+            for i, k0, k1 in rnd:
+                later = k0 > 0
+                att.append((q_rel[i], qls[i], krow, k1 - k0, lens[i] - qls[i], k0, q_rel[i], int(later)))
+                if later:
+                    fold.append((q_rel[i], q_rel[i], qls[i]))
+                krow += k1 - k0
+            if fold and tmp is None:
+                tmp = torch.empty_like(out)
+                tmp_lse = torch.empty_like(lse)
+            latent_ops.prefill_attention_varlen(q, k, v, att, self.scale, out, lse, tmp, tmp_lse, causal=True)
+            if fold:
+                latent_ops.attn_fold(out, lse, tmp, tmp_lse, fold)
+
+
+def plan_prefill_rounds(seq_lens, chunk: int) -> list:
+    """The key ranges a prefill step rebuilds, round by round: [(request index, k0, k1), ...] per round, at most
+    ``chunk`` keys in all per round (``chunk`` <= 0: one round of whole contexts). Every request's ranges cover
+    [0, seq_len) in order, the first starting at 0, at most one range of a request per round."""
+    if chunk <= 0:
+        return [[(i, 0, int(L)) for i, L in enumerate(seq_lens) if L > 0]]
+    rounds, cur, used = [], [], 0
+    for i, L in enumerate(seq_lens):
+        k = 0
+        while k < L:
+            take = min(int(L) - k, chunk - used)
+            cur.append((i, k, k + take))
+            used += take
+            k += take
+            if used == chunk:
+                rounds.append(cur)
+                cur, used = [], 0
+    if cur:
+        rounds.append(cur)
+    return rounds
 
 
 def latent_attention_step(impl: "LatentAttentionImpl", layer, query: torch.Tensor, hidden: torch.Tensor,

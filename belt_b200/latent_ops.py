@@ -103,6 +103,79 @@ def latent_rows_to_cache(c: torch.Tensor, slot_mapping: torch.Tensor, cache: tor
     torch.ops.lrkv_b200.cache_write(c, slot_mapping, cache, u_cat, segs, float(eps))
 
 
+def _check_kv_out(t: torch.Tensor, rows: int, name: str) -> None:
+    if t.dtype != torch.bfloat16 or tuple(t.shape) != (rows, 4, HEAD_DIM) or t.stride(2) != 1:
+        raise ValueError(f"{name} must be BF16 [{rows}, 4, 256] with contiguous channels")
+
+
+def decompress_varlen(cache: torch.Tensor, block_table: torch.Tensor, pieces, wk: torch.Tensor, k_segs,
+                      v_up_t: torch.Tensor, v_offset: int, cos_sin: torch.Tensor, k_out: torch.Tensor | None = None,
+                      v_out: torch.Tensor | None = None):
+    """Keys and values of several requests' position ranges in one launch: ``pieces`` = [(request row of
+    ``block_table``, its seq_len, pos0, count), ...]; piece i fills rows [sum of the earlier counts, + count) of
+    k_out / v_out [sum counts, 4, 256] (allocated when not given). Per piece the same result as
+    ``decompress_paged``."""
+    flat = [int(x) for pc in pieces for x in pc]
+    rows = sum(int(pc[3]) for pc in pieces)
+    dev = cache.device
+    if k_out is None:
+        k_out = torch.empty(rows, 4, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    if v_out is None:
+        v_out = torch.empty(rows, 4, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    if rows == 0:
+        return k_out, v_out
+    if cache.dtype != torch.bfloat16 or cache.stride(-1) != 1 or block_table.dtype != torch.int32 or \
+            block_table.stride(-1) != 1:
+        raise ValueError("decompress_varlen: BF16 cache with contiguous rows, int32 block table with contiguous rows")
+    _check_kv_out(k_out, rows, "k_out")
+    _check_kv_out(v_out, rows, "v_out")
+    if k_out.stride() != v_out.stride():
+        raise ValueError("decompress_varlen: k_out and v_out with the same strides")
+    torch.ops.lrkv_b200.decompress_varlen(cache, block_table, flat, wk, host_k_segs(k_segs), v_up_t, int(v_offset),
+                                          cos_sin, k_out, v_out)
+    return k_out, v_out
+
+
+def prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pieces, scale: float, out: torch.Tensor,
+                             lse: torch.Tensor, out2: torch.Tensor | None = None, lse2: torch.Tensor | None = None,
+                             causal: bool = True) -> None:
+    """Several pieces of prefill attention in one launch. q [Tq, 24, 256], k / v [Tk, 4, 256] BF16; ``pieces`` =
+    [(q_row, ql, k_row, S, q_pos0, k_pos0, o_row, to2), ...]: queries [q_row, q_row + ql) at positions q_pos0.. over
+    keys [k_row, k_row + S) at positions k_pos0.. (causal by position), written from row o_row of out / lse, or of
+    out2 / lse2 when to2 (same shapes and strides)."""
+    flat = [int(x) for pc in pieces for x in pc]
+    if not flat:
+        return
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1:
+            raise ValueError(f"prefill_attention_varlen: {name} [n, heads, 256] BF16 with contiguous channels")
+    if lse.dtype != torch.float32 or lse.stride(1) != 1:
+        raise ValueError("prefill_attention_varlen: lse [rows, 24] fp32 with contiguous heads")
+    if out2 is None:
+        out2, lse2 = out, lse
+    if out2.stride() != out.stride() or lse2.stride() != lse.stride():
+        raise ValueError("prefill_attention_varlen: out2 / lse2 with the strides of out / lse")
+    if out2 is out:
+        # one destination: the op's second pair may not alias the first, so give it an empty pair (no piece uses it)
+        if any(int(pc[7]) for pc in pieces):
+            raise ValueError("prefill_attention_varlen: a piece writes to out2, which was not given")
+        out2 = out.new_empty(0, out.shape[1], HEAD_DIM).as_strided((0, out.shape[1], HEAD_DIM), out.stride())
+        lse2 = lse.new_empty(0, lse.shape[1]).as_strided((0, lse.shape[1]), lse.stride())
+    torch.ops.lrkv_b200.prefill_attention_varlen(q, k, v, flat, float(scale), bool(causal), out, lse, out2, lse2)
+
+
+def attn_fold(out: torch.Tensor, lse: torch.Tensor, part: torch.Tensor, part_lse: torch.Tensor, pieces) -> None:
+    """Fold a chunk's attention result into the running one, in place, by log-sum-exp: ``pieces`` = [(destination row
+    of out / lse, source row of part / part_lse, rows), ...]."""
+    flat = [int(x) for pc in pieces for x in pc]
+    if not flat:
+        return
+    for name, t in (("out", out), ("part", part)):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[2] != HEAD_DIM or t.stride(2) != 1:
+            raise ValueError(f"attn_fold: {name} [rows, 24, 256] BF16 with contiguous channels")
+    torch.ops.lrkv_b200.attn_fold(out, lse, part, part_lse, flat)
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """x [M, K] @ weight[N, K]^T on the tensor cores (``belt_gemm_bf16``): BF16 operands with contiguous rows (any row
     strides that are multiples of 8), FP32 accumulation, BF16 out [M, N]. The model's linear layers (q_gate_proj,

@@ -63,6 +63,12 @@ class LatentLayer:
         return latent_ops.decompress_paged(cache, block_table_row, seq_len, pos0, count, self.wk, self.k_segs_host,
                                            self.v_up, self.v_offset, self.rope.cos_sin, k_out, v_out)
 
+    def decompress_varlen(self, cache: torch.Tensor, block_table: torch.Tensor, pieces, k_out=None, v_out=None):
+        """Keys and values of several requests' position ranges in one launch (``latent_ops.decompress_varlen``):
+        ``pieces`` = [(request row of ``block_table``, seq_len, pos0, count), ...], concatenated in that order."""
+        return latent_ops.decompress_varlen(cache, block_table, pieces, self.wk, self.k_segs_host, self.v_up,
+                                            self.v_offset, self.rope.cos_sin, k_out, v_out)
+
 
 def k_segs_rows(layout: dict) -> list:
     """[[start, length, start, length]] per group from the layout's ``k_segments`` (qwen3_5_latent.py:156-158)."""

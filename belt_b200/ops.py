@@ -25,6 +25,9 @@ Operators (mutated arguments marked !):
   up_project(a, v_up_t, out!)
   decompress(cache, block_table_row, seq_len, pos0, wk, k_segs, v_up_t, v_offset, cos_sin, k_out!, v_out!)
   prefill_attention(q, k, v, q_pos0, k_pos0, scale, causal, out!, lse!)
+  decompress_varlen(cache, block_table, pieces, wk, k_segs, v_up_t, v_offset, cos_sin, k_out!, v_out!)
+  prefill_attention_varlen(q, k, v, pieces, scale, causal, out!, lse!, out2!, lse2!)
+  attn_fold(out!, lse!, part, part_lse, pieces)
   linear(x, weight) -> x weight^T  (the model's linear layers, BF16)
 """
 
@@ -208,6 +211,50 @@ def _(q, k, v, q_pos0, k_pos0, scale, causal, out, lse):
     return None
 
 
+@custom_op(f"{NS}::decompress_varlen", mutates_args=("k_out", "v_out"), device_types="cuda")
+def decompress_varlen(cache: torch.Tensor, block_table: torch.Tensor, pieces: list[int], wk: torch.Tensor,
+                      k_segs: list[int], v_up_t: torch.Tensor, v_offset: int, cos_sin: torch.Tensor,
+                      k_out: torch.Tensor, v_out: torch.Tensor) -> None:
+    _lib.call("belt_latent_decompress_varlen", cache.data_ptr(), cache.shape[0], cache.shape[1], cache.shape[2],
+              cache.stride(0), cache.stride(1), block_table.data_ptr(), block_table.stride(0), len(pieces) // 4,
+              _lib.int_array(pieces), wk.data_ptr(), wk.shape[2], _lib.int_array(k_segs), v_up_t.data_ptr(),
+              int(v_offset), v_up_t.shape[1], cos_sin.data_ptr(), cos_sin.shape[0], k_out.data_ptr(), v_out.data_ptr(),
+              k_out.stride(0), k_out.stride(1), _err(cache), _stream(cache))
+
+
+@decompress_varlen.register_fake
+def _(cache, block_table, pieces, wk, k_segs, v_up_t, v_offset, cos_sin, k_out, v_out):
+    return None
+
+
+@custom_op(f"{NS}::prefill_attention_varlen", mutates_args=("out", "lse", "out2", "lse2"), device_types="cuda")
+def prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pieces: list[int], scale: float,
+                             causal: bool, out: torch.Tensor, lse: torch.Tensor, out2: torch.Tensor,
+                             lse2: torch.Tensor) -> None:
+    _lib.call("belt_prefill_attention_varlen", q.data_ptr(), q.shape[0], q.stride(0), q.stride(1), k.data_ptr(),
+              v.data_ptr(), k.shape[0], k.stride(0), k.stride(1), len(pieces) // 8, _lib.int_array(pieces),
+              int(bool(causal)), float(scale), out.data_ptr(), out2.data_ptr(), out.stride(0), out.stride(1),
+              lse.data_ptr(), lse2.data_ptr(), lse.stride(0), _err(q), _stream(q))
+
+
+@prefill_attention_varlen.register_fake
+def _(q, k, v, pieces, scale, causal, out, lse, out2, lse2):
+    return None
+
+
+@custom_op(f"{NS}::attn_fold", mutates_args=("out", "lse"), device_types="cuda")
+def attn_fold(out: torch.Tensor, lse: torch.Tensor, part: torch.Tensor, part_lse: torch.Tensor,
+              pieces: list[int]) -> None:
+    _lib.call("belt_attn_fold", out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), lse.stride(0),
+              part.data_ptr(), part.stride(0), part.stride(1), part_lse.data_ptr(), part_lse.stride(0),
+              len(pieces) // 3, _lib.int_array(pieces), _stream(out))
+
+
+@attn_fold.register_fake
+def _(out, lse, part, part_lse, pieces):
+    return None
+
+
 # ---------------------------------------------------------------------------------------------------------- linear
 @custom_op(f"{NS}::linear", mutates_args=(), device_types="cuda")
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
@@ -226,4 +273,5 @@ def _(x, weight):
 
 OPS = ("cache_write", "proj_cache_write", "decode_schedule", "latent_decode", "merge_segments", "merge_up_project",
        "block_diag_query",
-       "up_project", "decompress", "prefill_attention", "linear")
+       "up_project", "decompress", "prefill_attention", "decompress_varlen", "prefill_attention_varlen", "attn_fold",
+       "linear")

@@ -624,79 +624,92 @@ def run_gemm(args):
 
 
 def run_prefill(args):
-    """One c50 layer's prefill of an 8192-token request through the backend's kernels: decompress of the context
-    (keys and values from the paged rows) and the causal attention, timed on the device (inputs resident, L2 flushed
-    between steps); torch's scaled_dot_product_attention on the same keys and values timed beside it."""
+    """The prefill path of one c50 layer through the backend's varlen kernels, two workloads:
+
+    * ``single``: one request of 8192 new tokens over an 8192-token context (keys / values rebuilt from the paged rows,
+      causal attention): the line's headline;
+    * ``batched``: one step of four prefill requests of 2048, 4096, 8192 and 16384 new tokens each (whole prompts),
+      through ``LatentAttentionImpl._prefill``: one decompress launch and one attention launch for all four.
+
+    Timed on the device (inputs resident, L2 flushed before each step, NVML clocks sampled); torch's
+    scaled_dot_product_attention on the single request's keys and values beside it."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     from belt_b200 import build as _build
-    from belt_b200 import latent_ops
+    from belt_b200.latent_backend import LatentAttentionImpl, LatentAttentionMetadata
     from belt_b200.layer import derive_latent_tensors
     _build.build()
-    L, page = 8192, 16
+    page = 16
     w = synth.make_layer(synth.c50(), seed=synth.SEED_FACTORS)
-    lat = derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, synth.cos_sin_table(L + 1), device=dev)
-    bt, nb, _ = synth.block_tables([L], page, extra_blocks=1, seed=synth.SEED_CACHE)
-    W = w.layout["row_width"]
-    cache = torch.empty(nb, page, W, dtype=torch.bfloat16, device=dev)
-    synth.fill_cache(cache, w.layout, bt.to(dev), [L], seed=synth.SEED_CACHE, poison=False)
-    btd = bt.to(dev)
-    q = synth.make_queries(L).to(dev)
-    k = torch.empty(L, 4, 256, dtype=torch.bfloat16, device=dev)
-    v = torch.empty_like(k)
-    out = torch.empty(L, 24, 256, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(L, 24, device=dev)
+    lens_b = [2048, 4096, 8192, 16384]
+    max_len = max(lens_b)
+    lat = derive_latent_tensors(w.k_up, w.v_up, w.k_norm_weight, w.layout, synth.cos_sin_table(max_len + 1),
+                                device=dev)
+    impl = LatentAttentionImpl(H, D, SCALE, 4)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
-    def step():
-        lat.decompress_paged(cache, btd[0], L, 0, L, k, v)
-        latent_ops.prefill_attention(q, k, v, 0, 0, SCALE, True, out, lse)
+    def workload(lens, qls):
+        bt, nb, _ = synth.block_tables(lens, page, extra_blocks=1, seed=synth.SEED_CACHE)
+        cache = torch.empty(nb, page, w.layout["row_width"], dtype=torch.bfloat16, device=dev)
+        synth.fill_cache(cache, w.layout, bt.to(dev), lens, seed=synth.SEED_CACHE, poison=False)
+        m = LatentAttentionMetadata(num_actual_tokens=sum(qls), num_decodes=0, num_decode_tokens=0,
+                                    num_prefills=len(lens), num_prefill_tokens=sum(qls), block_table=bt.to(dev),
+                                    seq_lens=torch.tensor(lens, dtype=torch.int32, device=dev), sched=None)
+        m.prefill_q_len, m.prefill_seq_len = list(qls), list(lens)
+        q = torch.randn(sum(qls), H, D, device=dev, dtype=torch.bfloat16)
+        out = torch.empty(sum(qls), H, D, dtype=torch.bfloat16, device=dev)
+        return lambda: impl._prefill(lat, q, out, cache, m)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
+    def timed(step):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for s_, e_ in ev:
+            flush.add_(1)
+            s_.record()
+            step()
+            e_.record()
+        torch.cuda.synchronize()
+        return statistics.mean(s_.elapsed_time(e_) for s_, e_ in ev)
+
+    def flops(lens, qls):   # causal attention + the decompress of every context row
+        att = sum(24 * (ql * (L - ql) + ql * (ql + 1) / 2) * 256 * 4 for L, ql in zip(lens, qls))
+        return att + sum(lens) * 2 * 256 * 4 * (320 + 512)
+
+    clocks = ClockSampler(dev)
+    clocks.start()
+    L = 8192
+    ms = timed(workload([L], [L]))
+    ms_b = timed(workload(lens_b, lens_b))
+    clk = clocks.stop()
     dec.check_device_errors(dev)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for s, e in ev:
-        flush.add_(1)
-        s.record()
-        step()
-        e.record()
-    torch.cuda.synchronize()
-    ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    # torch's attention on the same shapes (one request), for comparison
+    q = torch.randn(L, H, D, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(L, 4, D, device=dev, dtype=torch.bfloat16)
     qh = q.transpose(0, 1).unsqueeze(0)
     kh = k.transpose(0, 1).repeat_interleave(6, 0).unsqueeze(0)
-    vh = v.transpose(0, 1).repeat_interleave(6, 0).unsqueeze(0)
     lib_ms = None
     try:
-        for _ in range(2):
-            torch.nn.functional.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=SCALE)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(3):
-            torch.nn.functional.scaled_dot_product_attention(qh, kh, vh, is_causal=True, scale=SCALE)
-        e.record()
-        torch.cuda.synchronize()
-        lib_ms = s.elapsed_time(e) / 3
+        lib_ms = timed(lambda: torch.nn.functional.scaled_dot_product_attention(qh, kh, kh, is_causal=True,
+                                                                                 scale=SCALE))
     except RuntimeError:
         pass
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except (OSError, ValueError):
-        pass
+    peaks = load_peaks()
     peak_tf = peaks.get("bf16_tflops") or 1590.0
-    flops = 24 * (L * (L + 1) / 2) * 256 * 2 * 2 + L * 2 * 256 * 4 * (320 + 512)   # attention + decompress
+    tf = flops([L], [L]) / (ms / 1e3) / 1e12
+    tf_b = flops(lens_b, lens_b) / (ms_b / 1e3) / 1e12
     line = {"metric": "prefill tokens/s (decompress + causal attention, one c50 layer)", "value": L / (ms / 1e3),
             "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "prefill: 8192 new tokens over an 8192-token context, c50 layer, page 16",
                        "l2": "flushed (256 MB write) before every step"},
-            "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12, "peak": peak_tf,
-                         "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / peak_tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": tf / peak_tf,
                          "peak_source": "measured" if "bf16_tflops" in peaks else "fallback"},
-            "library_sdpa_attention_ms": lib_ms, "gpu_launches": 2 * args.steps}
+            "batched": {"workload": "one step of 4 prefills of 2048, 4096, 8192, 16384 new tokens (whole prompts)",
+                        "ms_per_step": ms_b, "tokens_per_s": sum(lens_b) / (ms_b / 1e3), "tflops": tf_b,
+                        "frac": tf_b / peak_tf, "launches_per_step": 2},
+            "library_sdpa_attention_ms": lib_ms, "clocks": clk, "gpu_launches": 4 * (args.steps + max(args.warmup, 3))}
     print(json.dumps(line), flush=True)
 
 

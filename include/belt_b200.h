@@ -220,6 +220,46 @@ int belt_gemm_bf16(const void* a, int64_t m, int64_t k, int64_t lda, const void*
                    int64_t ldc, int32_t* err, void* stream);
 
 /*
+ * belt_latent_decompress over several pieces in one launch (the reference decompresses all prefill requests of a step
+ * together, latent_backend.py:214-225, 285-320). pieces: host int32 [num_pieces][4] = (request: row of block_table,
+ * seq_len, pos0, count); block_table [requests, >= pages] int32 with row stride bt_stride. The keys and values of
+ * piece i fill rows [sum of the earlier counts, + count_i) of k_out / v_out. Other arguments as belt_latent_decompress.
+ */
+int belt_latent_decompress_varlen(const void* cache, int64_t num_blocks, int32_t page, int32_t row_width,
+                                  int64_t stride_block, int64_t stride_tok, const int32_t* block_table,
+                                  int64_t bt_stride, int32_t num_pieces, const int32_t* pieces, const void* wk,
+                                  int32_t kc, const int32_t* k_segs, const void* v_up, int32_t v_offset, int32_t r_v,
+                                  const void* cos_sin, int32_t max_pos, void* k_out, void* v_out, int64_t out_st,
+                                  int64_t out_sg, int32_t* err, void* stream);
+
+/*
+ * belt_prefill_attention over several pieces in one launch: the reference's flash_attn_varlen_func calls over all
+ * prefill requests of a step (latent_backend.py:285-320). q [q_rows, 24, 256] and k / v [k_rows, 4, 256] are the
+ * concatenated queries and rebuilt keys / values; pieces: host int32 [num_pieces][8] = (q_row, ql, k_row, S, q_pos0,
+ * k_pos0, o_row, to2): queries [q_row, q_row + ql) at positions q_pos0.. over keys [k_row, k_row + S) at positions
+ * k_pos0.., causal by position; outputs and LSEs from row o_row of out / lse (to2 = 0) or of out2 / lse2 (to2 = 1;
+ * same strides). lse / lse2 may be NULL when no piece writes there.
+ */
+int belt_prefill_attention_varlen(const void* q, int64_t q_rows, int64_t q_st, int64_t q_sh, const void* k,
+                                  const void* v, int64_t k_rows, int64_t kv_st, int64_t kv_sg, int32_t num_pieces,
+                                  const int32_t* pieces, int32_t causal, float scale, void* out, void* out2,
+                                  int64_t out_st, int64_t out_sh, float* lse, float* lse2, int64_t lse_st,
+                                  int32_t* err, void* stream);
+
+/*
+ * The log-sum-exp fold of one chunk's attention result into the running one, in place: the reference merges every
+ * context chunk of its prefill into the output with vLLM's merge_attn_states (latent_backend.py:300-320).
+ * out [rows, 24, 256] BF16 (strides out_st, out_sh, 1), lse [rows, 24] fp32 (row stride lse_st); part / part_lse the
+ * chunk's output and LSE. pieces: host int32 [num_pieces][3] = (destination row, source row, rows). Per row and head:
+ * m = max(lse, plse), out = bf16((out e^(lse - m) + part e^(plse - m)) / (e^(lse - m) + e^(plse - m))),
+ * lse = m + log(e^(lse - m) + e^(plse - m)); a part row with LSE -inf leaves the row unchanged, a running row with LSE
+ * -inf takes the part row.
+ */
+int belt_attn_fold(void* out, int64_t out_st, int64_t out_sh, float* lse, int64_t lse_st, const void* part,
+                   int64_t part_st, int64_t part_sh, const float* part_lse, int64_t plse_st, int32_t num_pieces,
+                   const int32_t* pieces, void* stream);
+
+/*
  * The query side of the model's fused q-norm / RoPE (models/qwen3_5_latent.py:209-212, `fused_qk_rmsnorm_rope_gate`
  * with no key heads): qg [T, 24, >= 256] BF16 (element strides qg_st, qg_sh, 1; the query half of every head's
  * q_gate_proj block) -> q [T, 24, 256] BF16 = NeoX rotation of the first `rot` channels (BF16 cos / sin table

@@ -80,3 +80,17 @@ def test_reference_arm_on_the_cpu_runnable_config(capsys):
     assert line["impl"] == "reference" and line["extrapolated"] is False
     assert line["samples"]["timed_context_tokens_per_pass"] == 129 + 513 + 1025 + 2001
     assert line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_prefill_rounds_cover_every_context_once():
+    from belt_b200.latent_backend import plan_prefill_rounds
+    lens = [1000, 70, 450, 0, 384]
+    for chunk in (384, 100, 1, 5000, 0):
+        rounds = plan_prefill_rounds(lens, chunk)
+        for i, L in enumerate(lens):
+            ranges = [(k0, k1) for r in rounds for j, k0, k1 in r if j == i]
+            assert [k for rng in ranges for k in range(*rng)] == list(range(L)), (chunk, i)
+        for r in rounds:
+            assert len({j for j, _, _ in r}) == len(r)                       # a request at most once per round
+            if chunk > 0:
+                assert sum(k1 - k0 for _, k0, k1 in r) <= chunk

@@ -319,7 +319,9 @@ def test_merge_segments():
 
 def test_merge_up_project():
     """The fused merge + U_v projection against the two-kernel path (within 1 BF16 ulp: the same roundings, another
-    FP32 summation order in the projection) and against the oracle's merge followed by its projection (2 ulp)."""
+    FP32 summation order in the projection) and against the oracle's merge followed by its projection (2 ulp + 2e-3:
+    the merged output may differ from the oracle's by one BF16 ulp in some features, which moves outputs that nearly
+    cancel by more than their own ulp)."""
     g = torch.Generator().manual_seed(3)
     long = [int(x) for x in torch.randint(1, 3000, (70,), generator=g)]
     for seqs, nct, lv in [([129, 513, 1025, 2001], 16, 512), ([0, 300, 64, 0], 8, 96), ([40] * 40, 8, 640),
@@ -349,7 +351,7 @@ def test_merge_up_project():
         assert torch.allclose(lse.cpu()[live], lse2.cpu()[live], atol=1e-6, rtol=0), what
         ea, el = oracle.merge_segments(part, sched.seg_base.cpu(), B, lv)
         eo = oracle.up_project(ea.to(torch.bfloat16), v_up_t)
-        assert bf16_ulp_close(out.cpu(), eo, ulps=2, atol=1e-5), what
+        assert bf16_ulp_close(out.cpu(), eo, ulps=2, atol=2e-3), what
 
 
 # ------------------------------------------------------------------------------------------------- decode
@@ -685,15 +687,29 @@ def test_decompress_into_strided_views():
     assert_decompress_close(buf[:, 0].cpu(), buf[:, 1].cpu(), ek, ev, "strided views")
 
 
-def test_backend_forward_mixed_prefill():
+def test_backend_forward_mixed_prefill(monkeypatch):
     """Decodes and prefills in one step through the backend: every new token's row written, the decodes through the
-    split-KV kernel, the prefills' queries (several per request, the last positions of their contexts) attending
-    causally over keys and values rebuilt on the tensor cores, against the fp32 oracle (decompress + attention)."""
+    split-KV kernel, the prefills' queries (several per request, the last positions of their contexts; one request
+    entirely new) attending causally over keys and values rebuilt on the tensor cores, against the fp32 oracle
+    (decompress + attention). The four prefills take one decompress launch and one attention launch."""
+    import belt_b200.latent_backend as lb
+    calls = {"decompress": 0, "attention": 0}
+    real_d, real_a = latent_ops.decompress_varlen, latent_ops.prefill_attention_varlen
+
+    def count_d(*a, **k):
+        calls["decompress"] += 1
+        return real_d(*a, **k)
+
+    def count_a(*a, **k):
+        calls["attention"] += 1
+        return real_a(*a, **k)
+    monkeypatch.setattr(latent_ops, "decompress_varlen", count_d)
+    monkeypatch.setattr(lb.latent_ops, "prefill_attention_varlen", count_a)
     spec = synth.spec_from_ranks(448, 576)
     w = synth.make_layer(spec)
     lat, ref = layer_pair(w, max_pos=2100)
-    seqs = [300, 1, 129, 700, 2050]          # the last two are prefills of 37 and 300 new tokens
-    qlens = [1, 1, 1, 37, 300]
+    seqs = [300, 1, 129, 700, 2050, 520, 64]  # the last four are prefills of 37, 300, 20 and 64 new tokens
+    qlens = [1, 1, 1, 37, 300, 20, 64]
     page = 16
     bt, nb, _ = synth.block_tables(seqs, page, extra_blocks=2)
     W = w.layout["row_width"]
@@ -722,7 +738,7 @@ def test_backend_forward_mixed_prefill():
                                  block_table_tensor=bt.to(DEV), slot_mapping=slots.to(DEV), num_reqs=B,
                                  num_actual_tokens=T, max_query_len=max(qlens))
     md = builder.build(0, cm)
-    assert md.num_decodes == 3 and md.num_prefills == 2
+    assert md.num_decodes == 3 and md.num_prefills == 4
     impl = LatentAttentionImpl(24, 256, SCALE, 4)
 
     class Layer:
@@ -734,6 +750,7 @@ def test_backend_forward_mixed_prefill():
     dec.check_device_errors(DEV)
     assert bf16_ulp_close(kv_d[:, 0].cpu().view(-1, W)[slots], exp_cache.view(-1, W)[slots], ulps=1)
     assert_close_out(output, exp, "mixed prefill")
+    assert calls == {"decompress": 1, "attention": 1}, calls
 
 
 # ------------------------------------------------------------------------------------------------- prefill attention
@@ -793,7 +810,7 @@ def test_prefill_attention_strided_output():
 
 
 def test_backend_prefill_chunked_merge(monkeypatch):
-    """A prefill whose context spans several PREFILL_CHUNK chunks: the per-chunk attentions folded by log-sum-exp give
+    """A prefill whose context spans several PREFILL_CHUNK rounds: the per-round attentions folded by log-sum-exp give
     the whole-context result (the fp32 oracle)."""
     import belt_b200.latent_backend as lb
     monkeypatch.setattr(lb, "PREFILL_CHUNK", 384)
@@ -821,6 +838,124 @@ def test_backend_prefill_chunked_merge(monkeypatch):
     dec.check_device_errors(DEV)
     err = (out.float().cpu() - exp).abs()
     assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (float(err.max()), float(err.mean()))
+
+
+def test_backend_prefill_rounds_over_several_requests(monkeypatch):
+    """Three prefills whose contexts (1000, 70 and 450 tokens) are cut into rounds of 384 keys across requests: the
+    rounds' attentions folded by log-sum-exp give every request's whole-context result (the fp32 oracle)."""
+    import belt_b200.latent_backend as lb
+    monkeypatch.setattr(lb, "PREFILL_CHUNK", 384)
+    spec = synth.spec_from_ranks(512, 512)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=1100)
+    lens, qls, page = [1000, 70, 450], [70, 70, 33], 16
+    rounds = lb.plan_prefill_rounds(lens, 384)
+    assert len(rounds) == 4 and sum(k1 - k0 for r in rounds for _, k0, k1 in r) == sum(lens)
+    bt, nb, _ = synth.block_tables(lens, page, extra_blocks=1)
+    W = w.layout["row_width"]
+    kv = torch.zeros(nb, 1, page, W, dtype=torch.bfloat16)
+    synth.fill_cache(kv[:, 0], w.layout, bt, lens, seed=8, poison=False)
+    g = torch.Generator().manual_seed(16)
+    q = torch.randn(sum(qls), 24, 256, generator=g).to(torch.bfloat16)
+    exp = []
+    for b, (L, ql) in enumerate(zip(lens, qls)):
+        rows, rpos = oracle.gather_rows(kv[:, 0], bt, b, L)
+        k, v = oracle.decompress(ref, rows, rpos)
+        r0 = sum(qls[:b])
+        exp.append(_attention_fp32(q[r0:r0 + ql], k, v, L - ql, 0, SCALE)[0])
+    exp = torch.cat(exp)
+    m = lb.LatentAttentionMetadata(num_actual_tokens=sum(qls), num_decodes=0, num_decode_tokens=0, num_prefills=3,
+                                   num_prefill_tokens=sum(qls), block_table=bt.to(DEV),
+                                   seq_lens=torch.tensor(lens, dtype=torch.int32, device=DEV), sched=None)
+    m.prefill_q_len, m.prefill_seq_len = qls, lens
+    impl = LatentAttentionImpl(24, 256, SCALE, 4)
+    out = torch.zeros(sum(qls), 24, 256, dtype=torch.bfloat16, device=DEV)
+    impl._prefill(lat, q.to(DEV), out, kv.to(DEV)[:, 0], m)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    err = (out.float().cpu() - exp).abs()
+    assert float(err.max()) < MAX_ABS and float(err.mean()) < MEAN_ABS, (float(err.max()), float(err.mean()))
+
+
+def test_decompress_varlen_equals_per_request_launches():
+    """One varlen launch over pieces of three requests (whole contexts, a range inside a tile and a single position)
+    gives bit for bit the per-request launches' keys and values, concatenated."""
+    spec = synth.spec_from_ranks(448, 576)
+    w = synth.make_layer(spec)
+    lat, _ = layer_pair(w, max_pos=3000)
+    seqs = [2049, 1, 700]
+    batch = synth.make_batch(w.layout, seqs, page=16, seed=33)
+    cache, bt = batch.cache.to(DEV), batch.block_table.to(DEV)
+    pieces = [(0, 2049, 0, 2049), (1, 1, 0, 1), (2, 700, 37, 600), (0, 2049, 1000, 1), (2, 700, 699, 1)]
+    k, v = lat.decompress_varlen(cache, bt, pieces)
+    ks, vs = [], []
+    for b, L, pos0, count in pieces:
+        kb, vb = lat.decompress_paged(cache, bt[b], L, pos0, count)
+        ks.append(kb)
+        vs.append(vb)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    assert torch.equal(k.view(torch.int16), torch.cat(ks).view(torch.int16))
+    assert torch.equal(v.view(torch.int16), torch.cat(vs).view(torch.int16))
+
+
+def test_prefill_attention_varlen_equals_per_piece_launches():
+    """One varlen attention launch over four pieces (causal prefixes, a chunk that sees a prefix of its keys, a piece
+    written to the second output) gives bit for bit the per-piece launches."""
+    g = torch.Generator().manual_seed(17)
+    qls, Ss = [37, 200, 1, 130], [700, 500, 1, 256]
+    qp0, kp0 = [663, 1000, 0, 0], [0, 300, 0, 100]
+    q = torch.randn(sum(qls), 24, 256, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(sum(Ss), 4, 256, generator=g).to(torch.bfloat16).to(DEV)
+    v = torch.randn(sum(Ss), 4, 256, generator=g).to(torch.bfloat16).to(DEV)
+    out = torch.zeros(sum(qls), 24, 256, dtype=torch.bfloat16, device=DEV)
+    lse = torch.zeros(sum(qls), 24, device=DEV)
+    out2, lse2 = torch.zeros_like(out), torch.zeros_like(lse)
+    pieces, qr, kr = [], 0, 0
+    for i in range(4):
+        pieces.append((qr, qls[i], kr, Ss[i], qp0[i], kp0[i], qr, int(i == 1)))
+        qr += qls[i]
+        kr += Ss[i]
+    latent_ops.prefill_attention_varlen(q, k, v, pieces, SCALE, out, lse, out2, lse2)
+    torch.cuda.synchronize()
+    dec.check_device_errors(DEV)
+    for i, (q_row, ql, k_row, S, q_pos0, k_pos0, o_row, to2) in enumerate(pieces):
+        o1, l1 = latent_ops.prefill_attention(q[q_row:q_row + ql], k[k_row:k_row + S], v[k_row:k_row + S], q_pos0,
+                                              k_pos0, SCALE, causal=True)
+        dst, dl = (out2, lse2) if to2 else (out, lse)
+        assert torch.equal(dst[o_row:o_row + ql].view(torch.int16), o1.view(torch.int16)), i
+        assert torch.equal(dl[o_row:o_row + ql], l1), i
+
+
+def test_attn_fold():
+    """The log-sum-exp fold against its fp32 restatement, with rows where the part saw no key (-inf: unchanged) and
+    rows whose running result is empty (-inf: replaced)."""
+    g = torch.Generator().manual_seed(18)
+    R = 50
+    out = torch.randn(R, 24, 256, generator=g).to(torch.bfloat16)
+    part = torch.randn(R + 10, 24, 256, generator=g).to(torch.bfloat16)
+    lse = torch.randn(R, 24, generator=g) * 3
+    plse = torch.randn(R + 10, 24, generator=g) * 3
+    lse[3, 5] = float("-inf")
+    plse[10 + 7, 2] = float("-inf")
+    pieces = [(0, 10, 20), (20, 30, 30)]
+    o_d, l_d = out.to(DEV), lse.to(DEV)
+    latent_ops.attn_fold(o_d, l_d, part.to(DEV), plse.to(DEV), pieces)
+    torch.cuda.synchronize()
+    exp_o, exp_l = out.float().clone(), lse.clone()
+    for dst, src, n in pieces:
+        for i in range(n):
+            lo, lc = lse[dst + i], plse[src + i]
+            m = torch.maximum(lo, lc)
+            wo, wc = torch.exp(lo - m).nan_to_num(0.0), torch.exp(lc - m).nan_to_num(0.0)
+            merged = (out[dst + i].float() * wo[:, None] + part[src + i].float() * wc[:, None]) / (wo + wc)[:, None]
+            keep = torch.isinf(lc)
+            take = torch.isinf(lo) & ~keep
+            exp_o[dst + i] = torch.where(keep[:, None], out[dst + i].float(),
+                                         torch.where(take[:, None], part[src + i].float(), merged))
+            exp_l[dst + i] = torch.where(keep, lo, torch.where(take, lc, m + torch.log(wo + wc)))
+    assert bf16_ulp_close(o_d.cpu(), exp_o.to(torch.bfloat16), ulps=1, atol=1e-6)
+    assert torch.allclose(l_d.cpu(), exp_l, atol=1e-5, rtol=0)
 
 
 # ------------------------------------------------------------------------------------------------- model-side block
