@@ -25,15 +25,15 @@ namespace {
 constexpr int kMuThreads = 1024;
 constexpr int kMuReqs = 32;                         // requests per CTA (the MMA's N)
 constexpr int kMuStageBytes = 4 * 64 * 128;         // 256 channels x 64 k x 2 B = 32 KB
-constexpr int kMuStages = 3;
+constexpr int kMuStages = 5;                        // 160 KB: five of the (at most ten) K blocks in flight
 constexpr int kMuMaxChunks = 10;                    // r_v <= 640
 constexpr int kMuBChunk = kMuReqs * 128;            // 32 requests x 64 k x 2 B = 4 KB per K block
-constexpr int kMuOffB = kMuStages * kMuStageBytes;  // 96 KB
+constexpr int kMuOffB = kMuStages * kMuStageBytes;  // 160 KB
 constexpr int kMuOffW = kMuOffB + kMuMaxChunks * kMuBChunk;   // per-warp segment weights
 constexpr int kMuWeights = 64;                      // segment weights staged per pass, per warp (more than 32)
 constexpr int kMuOffBars = kMuOffW + (kMuThreads / 32) * kMuWeights * 4;
-// barriers: full[3], empty[3], done
-constexpr int uFull = 0, uEmpty = 3, uDone = 6, kMuBars = 7;
+// barriers: full[5], empty[5], done
+constexpr int uFull = 0, uEmpty = kMuStages, uDone = 2 * kMuStages, kMuBars = 2 * kMuStages + 1;
 
 // Offset of element (row, k) of a K-major 128-byte-swizzled operand of 64-column chunks of `rows` rows.
 __device__ __forceinline__ int sw128_elem(int row, int k, int rows) {
