@@ -326,6 +326,13 @@ __device__ __forceinline__ void warpgroup_reg_dealloc() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Programmatic dependent launch. A kernel launched with launch_after() may start before the kernel ahead of it in the
+// stream has finished; grid_dependency_wait() blocks the calling thread until that kernel has completed and its
+// memory is visible (it returns at once when there is no such kernel). allow_dependents_launch() lets the next
+// kernel, if launched that way, start launching now.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

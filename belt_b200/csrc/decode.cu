@@ -246,6 +246,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the next kernel (the segment merge) may start launching; it waits for this grid before it reads the partials
+  if (threadIdx.x == 0) allow_dependents_launch();
 
   if (warp < 4) {
    warpgroup_reg_dealloc<kRegsWg0>();
@@ -492,6 +494,9 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     // block-diagonal query chunks, one per lane, as soon as the previous segment's last RoPE score released them
     if (lane < kProducerLanes && has_work) {
       constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
+      // the query comes from the kernel ahead of this one (the absorbed-query GEMM), which may still be running; every
+      // global write of this kernel (the partials) comes after the query, so after this wait as well
+      grid_dependency_wait();
       int qsegs = 0;
       TileCursor c;
       c.begin(p, seg_begin, seg_end);
@@ -802,8 +807,8 @@ cudaError_t launch_latent_decode(const DecodeMaps& maps, const DecodeParams& p, 
     if (e != cudaSuccess) return e;
     attr_done[m][dev] = true;
   }
-  kernel<<<num_ctas, dec::kThreads, p.smem_bytes, stream>>>(maps, p);
-  return cudaGetLastError();
+  cudaError_t e = launch_after(kernel, dim3(num_ctas), dim3(dec::kThreads), p.smem_bytes, stream, maps, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace belt

@@ -63,7 +63,11 @@ __global__ void __launch_bounds__(kHgThreads, 1)
   __nv_bfloat16* out_row = p.Out + static_cast<long long>(row) * p.sot + static_cast<long long>(h) * p.soh;
 
   const Runs runs(p, g);
+  // X comes from the kernel ahead of this one, which may still be running, and Out may reuse memory it reads: wait for
+  // it before any global access but the weights'
+  if (threadIdx.x == 0) allow_dependents_launch();
   if (runs.all_dead(n0, n0 + BN)) {   // no live column: zeros (uniform over the CTA, before any barrier or TMEM use)
+    grid_dependency_wait();
     if (row < p.T) {
       if (p.vec_out && n0 + BN <= p.N) {
         uint4* dst = reinterpret_cast<uint4*>(out_row + n0);
@@ -97,6 +101,7 @@ __global__ void __launch_bounds__(kHgThreads, 1)
 
   if (threadIdx.x == 0) {
     // ---------------------------------------------------------------- producer
+    grid_dependency_wait();
     int issued = 0;
     for (int k = 0; k < nk; ++k) {
       const int s = k % S;
@@ -204,22 +209,22 @@ cudaError_t launch_head_gemm(const HeadGemmMaps& maps, HeadGemmParams p, cudaStr
     case 1:
       e = cudaFuncSetAttribute(head_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      head_gemm_kernel<1><<<grid, kHgThreads, smem, stream>>>(maps, p);
+      e = launch_after(head_gemm_kernel<1>, grid, dim3(kHgThreads), smem, stream, maps, p);
       break;
     case 2:
       e = cudaFuncSetAttribute(head_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      head_gemm_kernel<2><<<grid, kHgThreads, smem, stream>>>(maps, p);
+      e = launch_after(head_gemm_kernel<2>, grid, dim3(kHgThreads), smem, stream, maps, p);
       break;
     case 4:
       e = cudaFuncSetAttribute(head_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       if (e != cudaSuccess) return e;
-      head_gemm_kernel<4><<<grid, kHgThreads, smem, stream>>>(maps, p);
+      e = launch_after(head_gemm_kernel<4>, grid, dim3(kHgThreads), smem, stream, maps, p);
       break;
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace belt

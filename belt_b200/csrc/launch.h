@@ -307,6 +307,24 @@ cudaError_t launch_gemm(const GemmMaps& maps, GemmParams p, int num_sms, cudaStr
 // Bounded-wait self-test (selftest.cu).
 cudaError_t launch_selftest_wait(int* err, int* status, cudaStream_t stream);
 
+// Launches `kernel` so that it may start while the kernel ahead of it in `stream` is still running (programmatic
+// dependent launch): it must call grid_dependency_wait() before it reads anything that kernel writes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_after(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                         Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Sets the text belt_last_error() returns on the calling thread.
 void set_last_error(const char* msg);
 

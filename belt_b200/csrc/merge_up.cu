@@ -83,6 +83,10 @@ __global__ void __launch_bounds__(kMuThreads, 1)
   // zero the operand first: feature columns past r_v must be 0 (U_v's zero-filled rows meet them)
   for (int i = threadIdx.x; i < nk * kMuBChunk / 16; i += kMuThreads)
     reinterpret_cast<uint4*>(sB)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x == 0) allow_dependents_launch();
+  // the partials come from the decode kernel ahead of this one, which may still be running (U_v, a weight, was
+  // requested above); nothing of this kernel touches global memory other than U_v before this wait
+  grid_dependency_wait();
   __syncthreads();
   float* wts = wts_all + warp * kMuWeights;
   {
@@ -235,8 +239,8 @@ cudaError_t launch_merge_up(const MergeUpMaps& maps, const MergeUpParams& p, cud
   cudaError_t e = cudaFuncSetAttribute(merge_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(p.nh, (p.num_reqs + kMuReqs - 1) / kMuReqs);
-  merge_up_kernel<<<grid, kMuThreads, smem, stream>>>(maps, p);
-  return cudaGetLastError();
+  e = launch_after(merge_up_kernel, grid, dim3(kMuThreads), smem, stream, maps, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace belt
