@@ -49,6 +49,7 @@ SIGNATURES = {
     "belt_gemm_bf16": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp],
     "belt_selftest_bounded_wait": [c_vp, c_vp, c_vp],
     "belt_num_sms": [c_i32],
+    "belt_path_counts": [c_vp, c_i32],
     "belt_abi_version": [],
 }
 
@@ -96,3 +97,10 @@ def call(name: str, *args) -> None:
 def int_array(values) -> ctypes.Array:
     vals = [int(v) for v in values]
     return (ctypes.c_int32 * len(vals))(*vals)
+
+
+def path_counts() -> dict:
+    """Launches that took a CUDA-core fallback because TMA could not describe the operands (``belt_path_counts``)."""
+    out = (ctypes.c_int64 * 2)()
+    call("belt_path_counts", ctypes.cast(out, ctypes.c_void_p), 2)
+    return {"simt_group_gemm": int(out[0]), "simt_cache_write": int(out[1])}

@@ -1,4 +1,5 @@
 // The C ABI (include/belt_b200.h): argument checks, TMA descriptor encoding and kernel launches.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -11,6 +12,10 @@
 namespace {
 
 thread_local std::string g_last_error;
+
+// Launches that took a CUDA-core kernel because TMA could not describe the operands (see belt_path_counts).
+std::atomic<long long> g_simt_group_gemm{0};
+std::atomic<long long> g_simt_cache_write{0};
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -116,6 +121,7 @@ int run_group_product(const belt::GroupGemmParams& gp, const char* what, int32_t
     e = belt::launch_head_gemm(maps, hp, stream);
   } else {
     e = belt::launch_group_gemm(gp, stream);
+    g_simt_group_gemm.fetch_add(1, std::memory_order_relaxed);
   }
   if (e != cudaSuccess) {
     char buf[96];
@@ -133,7 +139,15 @@ extern "C" {
 
 const char* belt_last_error(void) { return g_last_error.c_str(); }
 
-int belt_abi_version(void) { return 200; }
+int belt_abi_version(void) { return 201; }
+
+int belt_path_counts(int64_t* counts, int32_t n) {
+  if (!counts || n < 0) return fail(BELT_ERR_INVALID, "path_counts: null buffer");
+  const long long v[2] = {g_simt_group_gemm.load(std::memory_order_relaxed),
+                          g_simt_cache_write.load(std::memory_order_relaxed)};
+  for (int i = 0; i < n && i < 2; ++i) counts[i] = v[i];
+  return ok();
+}
 
 int belt_num_sms(int32_t device) {
   int n = 0;
@@ -347,6 +361,7 @@ int belt_latent_rows_to_cache(const void* c, int64_t num_tokens, int64_t c_st, c
       return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
     }
   }
+  g_simt_cache_write.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = belt::launch_cache_write(p, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_rows_to_cache launch");
 }

@@ -157,6 +157,7 @@ class _ErrorWatch:
     def poll(self) -> None:
         if torch.cuda.is_current_stream_capturing():
             return
+        _warn_on_fallbacks()
         if self.armed:
             if not self.landed.query():
                 return                              # the GPU is still behind: read at a later build
@@ -171,6 +172,23 @@ class _ErrorWatch:
         self.host.copy_(dec.error_word(self.device), non_blocking=True)
         self.landed.record(stream)
         self.armed = True
+
+
+_FALLBACKS_SEEN: dict = {}
+
+
+def _warn_on_fallbacks() -> None:
+    """Warn once per kind when a launch took a CUDA-core fallback (operands TMA cannot describe: a strided query or
+    latent view with rows not 16-byte aligned, a group over more than five 64-column chunks). The results are correct;
+    the fallback is slower."""
+    import warnings
+    from . import _lib
+    for kind, n in _lib.path_counts().items():
+        if n > _FALLBACKS_SEEN.get(kind, 0):
+            if kind not in _FALLBACKS_SEEN:
+                warnings.warn(f"belt_b200: {n} launch(es) took the CUDA-core fallback ({kind}): the operands' strides or "
+                              "alignment cannot be described by TMA", RuntimeWarning, stacklevel=3)
+            _FALLBACKS_SEEN[kind] = n
 
 
 def _error_watch(device: torch.device) -> _ErrorWatch:

@@ -29,8 +29,18 @@ extern "C" {
 /* Thread-local description of the last failure of a belt_* call on this thread ("" if none). */
 const char* belt_last_error(void);
 
-/* ABI version of this library (major * 100 + minor). 200: the per-head GEMM entry points take an error word. */
+/* ABI version of this library (major * 100 + minor). 200: the per-head GEMM entry points take an error word;
+ * 201: belt_path_counts. */
 int belt_abi_version(void);
+
+/*
+ * Host-side counts, since the library was loaded, of the launches that ran a CUDA-core kernel because TMA could not
+ * describe the operands (no counterpart in the reference): counts[0] = belt_block_diag_query / belt_up_project calls
+ * that took the SIMT group GEMM (strides not multiples of 16 bytes, a misaligned base), counts[1] =
+ * belt_latent_rows_to_cache calls that took the SIMT cache write (a group over more than five 64-column chunks, a
+ * misaligned u_cat). Writes min(n, 2) counts. The results are the same either way; the counts say which path ran.
+ */
+int belt_path_counts(int64_t* counts, int32_t n);
 
 /*
  * Split-KV schedule of one decode step: replaces cute_decode.py:601-607 (`schedule`) / :571-598 (`_schedule`).

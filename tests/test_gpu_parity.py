@@ -12,7 +12,7 @@ import torch
 
 import oracle
 from belt_b200 import decode as dec
-from belt_b200 import latent_ops, synth
+from belt_b200 import _lib, latent_ops, synth
 from belt_b200.latent_backend import (CommonAttentionMetadata, LatentAttentionImpl, LatentAttentionMetadataBuilder,
                                       LatentKVSpec, latent_attention_step)
 from belt_b200.layer import derive_latent_tensors
@@ -169,8 +169,10 @@ def test_cache_write_prefill_chunk_and_unaligned_inputs():
         slots[::11] = -1
         cache = torch.zeros(nb, page, W, dtype=torch.bfloat16, device=DEV)
         c_dev = c_full.to(DEV)[:, c_off:c_off + W]
+        before = _lib.path_counts()["simt_cache_write"]
         latent_ops.latent_rows_to_cache(c_dev, slots.to(DEV), cache, u_cat, lat.k_segs, 1e-6)
         torch.cuda.synchronize()
+        assert _lib.path_counts()["simt_cache_write"] == before + (u_cat is u_off)     # only the misaligned u_cat
         live = torch.nonzero(slots >= 0).flatten()
         sample = live[torch.randperm(live.numel(), generator=g)[:256]]
         exp = oracle.latent_rows(c[sample], slots[sample], torch.zeros(nb, page, W, dtype=torch.bfloat16),
@@ -281,6 +283,26 @@ def test_block_diag_query(name):
     assert bf16_ulp_close(got, fx["q_bd"], ulps=1)
     dense = latent_ops.block_diag_query(q.to(DEV), lat.qmap).cpu()  # the full product gives the same query
     assert bf16_ulp_close(dense, exp, ulps=1)
+
+
+def test_block_diag_query_fallback_is_counted():
+    """A query whose token stride is not a multiple of 16 bytes cannot be described by TMA: the product runs on the
+    CUDA-core kernel, gives the same values, and the library's path count says so."""
+    fx, spec, w, batch, q = golden_case(CASES[0])
+    lat, ref = layer_pair(w)
+    T = q.shape[0]
+    buf = torch.zeros(T, 24 * 256 + 1, dtype=torch.bfloat16, device=DEV)
+    q_odd = buf.as_strided((T, 24, 256), (24 * 256 + 1, 256, 1))
+    q_odd.copy_(q)
+    before = _lib.path_counts()
+    got = lat.block_diag_query(q_odd).cpu()
+    after = _lib.path_counts()
+    assert after["simt_group_gemm"] == before["simt_group_gemm"] + 1
+    assert after["simt_cache_write"] == before["simt_cache_write"]
+    assert bf16_ulp_close(got, oracle.block_diag_query(q, ref["qmap"]), ulps=1)
+    before = after
+    lat.block_diag_query(q.to(DEV))
+    assert _lib.path_counts() == before                       # the aligned query stays on the tensor cores
 
 
 @pytest.mark.parametrize("name", CASES)
