@@ -94,13 +94,13 @@ def workload_spec(config: int, batch: int | None, rank: int, world: int, rows: s
             "workload": "config1: 1 layer c50, 4 requests with contexts {128, 512, 1024, 2000} + this step's, page 16"}
     if config == 2:
         B = batch or 64
-        return [synth.c50()], [8192 + 1] * B, 16, {"workload": "config2: 1 layer c50, batch 64 x 8192, page 16"}
+        return [synth.c50()], [8192 + 1] * B, 16, {"workload": f"config2: 1 layer c50, batch {B} x 8192, page 16"}
     if config == 4:
         # long context: every request 65,536 cached tokens + this step's, 512 tiles each over the CTAs
         B = batch or 32
         spec = synth.c25() if rows == "c25" else synth.c50()
         return [spec] * 16, [65536 + 1] * B, 16, {
-            "workload": f"config4: 16 layers {rows} (rows of {spec.row_width} columns), batch 32 x 65536, page 16"}
+            "workload": f"config4: 16 layers {rows} (rows of {spec.row_width} columns), batch {B} x 65536, page 16"}
     ranks = synth.learned_ranks(16)
     specs = [synth.spec_from_ranks(rk, rv) for rk, rv in ranks]
     if config == 5:
@@ -111,7 +111,7 @@ def workload_spec(config: int, batch: int | None, rank: int, world: int, rows: s
     B = batch or 128
     lens = synth.log_uniform_lengths(B, 1024, 65536, seed=synth.SEED_LENGTHS)
     return specs, [L + 1 for L in lens], 16, {
-        "workload": "config3: 16 layers, learned ranks (r_k in {384..640}, r_v = 1024 - r_k), batch 128/GPU, "
+        "workload": f"config3: 16 layers, learned ranks (r_k in {{384..640}}, r_v = 1024 - r_k), batch {B}/GPU, "
                     "context log-uniform [1k, 64k], page 16"}
 
 
