@@ -949,6 +949,8 @@ int belt_merge_up_project(const float* part, int64_t part_ss, int64_t part_sh, c
     return fail(BELT_ERR_INVALID, "merge_up_project: part strides, v_up_t alignment or lse stride");
   MergeUpParams p{part, part_ss, part_sh, seg_base, num_reqs, kH, kHPG, lv, static_cast<__nv_bfloat16*>(out),
                   out_st, out_sh, lse, lse_sb, err};
+  p.vec_part = aligned16(part) && part_ss % 4 == 0 && part_sh % 4 == 0 && lv % 4 == 0;
+  p.vec_out = aligned16(out) && out_st % 8 == 0 && out_sh % 8 == 0;
   MergeUpMaps maps;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(lv), static_cast<cuuint64_t>(kG)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(lv) * kD * 2};

@@ -132,6 +132,8 @@ struct MergeUpParams {
   float* lse;          // may be null
   long long slb;
   int* err;
+  int vec_part;        // part rows 16-byte aligned and lv % 4 == 0: float4 loads of the partial rows
+  int vec_out;         // out 16-byte aligned, strides multiples of 8: 16-byte stores
 };
 cudaError_t launch_merge_up(const MergeUpMaps& maps, const MergeUpParams& p, cudaStream_t stream);
 

@@ -9,13 +9,19 @@
 // One CTA per (head, tile of 32 requests), 1024 threads (a warp per request):
 //   * thread 0 streams U_v^T of the head's group ([r_v, 256], channels contiguous) in 64-deep K blocks, four boxes of
 //     64 channels x 64 k (MN-major, 128-byte swizzle) per stage, from the start (it does not depend on the merge);
-//   * warp j merges request j: its lanes reduce the segment LSEs in one pass (a running max and sum per lane, then
-//     across the warp), then sweep the r_v features (coalesced rows of part, the rows of up to four segments in flight
-//     together) and write a as the K-major B operand (32 requests x r_v, 128-byte swizzle);
+//   * warp j merges request j: its lanes reduce the segment LSEs (a running max and sum per lane, then across the
+//     warp) and write a as the K-major B operand (32 requests x r_v, 128-byte swizzle). With 16-byte aligned partial
+//     rows (the backend pads their stride to a multiple of 4 floats) a lane owns 4 consecutive features per 128 and
+//     loads them as float4, two segments' rows in flight at once, the first two issued together with the LSE loads;
+//     otherwise the rows are swept with scalar loads, four segments in flight;
 //   * thread 32 issues tcgen05 out^T[channel, request] += U_v^T[channel, k] a^T[k, request]: M = 128 channels (two
 //     halves), N = 32 requests, K = 16 per instruction, into TMEM;
-//   * epilogue (warps 0-3): thread (warp w, lane l) holds channel 32 w + l of both halves for the 32 requests; a warp's
+//   * epilogue (warps 0-3): thread (warp w, lane l) holds channel 32 w + l of both halves for the 32 requests; with an
+//     aligned output it stages them as [request][256 channels] BF16 in the (consumed) first ring stage and every
+//     thread of the CTA then stores 16 bytes (one request row = 512 contiguous bytes per warp); otherwise a warp's
 //     stores of one request cover 32 consecutive channels (64 bytes).
+// The U_v K blocks past the ring's first fill are prefetched into L2 at the start, so that their reloads after the
+// merge come from L2.
 #include "common.cuh"
 #include "launch.h"
 
@@ -39,6 +45,85 @@ constexpr int uFull = 0, uEmpty = kMuStages, uDone = 2 * kMuStages, kMuBars = 2 
 __device__ __forceinline__ int sw128_elem(int row, int k, int rows) {
   const int c = k >> 6, kk = k & 63;
   return c * rows * 128 + row * 128 + ((((kk >> 3) ^ (row & 7)) << 4) | ((kk & 7) << 1));
+}
+// One pass of the float4 merge over features [f0, f0 + 128 NQ): lane l owns f0 + 128 q + 4 l .. + 3. v holds the
+// first two segments' rows when the caller issued them; acc = fma(w_s, v_s, acc) over s in order, a = bf16(acc / d).
+template <int NQ>
+struct VecPass {
+  float4 v[2][NQ];
+  __device__ __forceinline__ void load(const MergeUpParams& p, const float* base, int n, int s, int f0, int lane) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int f = f0 + 128 * q + 4 * lane;
+        v[u][q] = (s + u < n && f < p.lv)
+                      ? __ldg(reinterpret_cast<const float4*>(base + static_cast<long long>(s + u) * p.ps + f))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+  }
+  // v holds segments 0 and 1 on entry
+  __device__ __forceinline__ void run(const MergeUpParams& p, const float* base, int n, int f0, int lane, float my_w,
+                                      float inv, int j, uint8_t* sB) {
+    float4 acc[NQ];
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < n; s += 2) {
+      if (s > 0) load(p, base, n, s, f0, lane);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float w = __shfl_sync(0xffffffffu, my_w, (s + u) & 31);
+        if (s + u < n) {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            acc[q].x = fmaf(w, v[u][q].x, acc[q].x);
+            acc[q].y = fmaf(w, v[u][q].y, acc[q].y);
+            acc[q].z = fmaf(w, v[u][q].z, acc[q].z);
+            acc[q].w = fmaf(w, v[u][q].w, acc[q].w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < NQ; ++q) {
+      const int f = f0 + 128 * q + 4 * lane;
+      if (f < p.lv) {
+        uint2 pk;
+        pk.x = pack_bf16(acc[q].x * inv, acc[q].y * inv);
+        pk.y = pack_bf16(acc[q].z * inv, acc[q].w * inv);
+        *reinterpret_cast<uint2*>(sB + sw128_elem(j, f, kMuReqs)) = pk;   // 4 features: 8 bytes of a 16-byte unit
+      }
+    }
+  }
+};
+
+// Merge of request b's n <= 32 segments for head h into row j of the B operand, float4 path (16-byte aligned rows,
+// lv % 4 == 0): the same arithmetic and order as the scalar sweep (and belt_merge_segments): m = max of the LSEs,
+// d = warp sum of exp(lse_s - m), a = bf16(sum_s exp(lse_s - m) v_s / d) accumulated by fma in segment order. The first
+// two segments' rows are loaded together with the LSEs; NQ1 (+ NQ2) float4 columns a lane, two passes for wide rows so
+// that two segments stay in flight within the 64 registers a thread has at 1,024 threads.
+template <int NQ1, int NQ2>
+__device__ __forceinline__ void merge_rows_vec(const MergeUpParams& p, const float* base, int n, int b, int h, int j,
+                                               int lane, uint8_t* sB) {
+  const float l_me = lane < n ? __ldg(base + static_cast<long long>(lane) * p.ps + p.lv) : -INFINITY;
+  VecPass<NQ1> a;
+  a.load(p, base, n, 0, 0, lane);
+  float m = l_me;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float my_w = lane < n ? __expf(l_me - m) : 0.f;   // lane s: the weight of segment s
+  float d = my_w;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+  const bool has = d > 0.f;
+  const float inv = has ? 1.f / d : 0.f;
+  if (lane == 0 && p.lse) p.lse[static_cast<long long>(b) * p.slb + h] = has ? m + __logf(d) : -INFINITY;
+  a.run(p, base, n, 0, lane, my_w, inv, j, sB);
+  if constexpr (NQ2 > 0) {
+    VecPass<NQ2> c;
+    c.load(p, base, n, 0, 128 * NQ1, lane);
+    c.run(p, base, n, 128 * NQ1, lane, my_w, inv, j, sB);
+  }
 }
 }  // namespace
 
@@ -76,8 +161,12 @@ __global__ void __launch_bounds__(kMuThreads, 1)
 #pragma unroll
     for (int q = 0; q < 4; ++q) tma_load_3d(st + q * 8192, &maps.v, &bars[uFull + s], 64 * q, 64 * k, g);
   };
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
     for (; issued < nk && issued < kMuStages; ++issued) produce(issued);
+    for (int k = issued; k < nk; ++k)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tma_prefetch_l2_3d(&maps.v, 64 * q, 64 * k, g);
+  }
 
   // ---------------------------------------------------------------- merge into the B operand
   // zero the operand first: feature columns past r_v must be 0 (U_v's zero-filled rows meet them)
@@ -94,6 +183,15 @@ __global__ void __launch_bounds__(kMuThreads, 1)
     if (b < p.num_reqs) {
       const int s0 = __ldg(p.seg_base + b), n = __ldg(p.seg_base + b + 1) - s0;
       const float* base = p.part + static_cast<long long>(s0) * p.ps + static_cast<long long>(h) * p.ph;
+      if (p.vec_part && n <= 32) {
+        switch ((p.lv + 127) >> 7) {
+          case 1: merge_rows_vec<1, 0>(p, base, n, b, h, j, lane, sB); break;
+          case 2: merge_rows_vec<2, 0>(p, base, n, b, h, j, lane, sB); break;
+          case 3: merge_rows_vec<3, 0>(p, base, n, b, h, j, lane, sB); break;
+          case 4: merge_rows_vec<4, 0>(p, base, n, b, h, j, lane, sB); break;
+          default: merge_rows_vec<3, 2>(p, base, n, b, h, j, lane, sB); break;
+        }
+      } else {
       // the segment LSEs' max, then the sum of their exponentials (the order and arithmetic of belt_merge_segments,
       // so that the merged output rounds the same way)
       float m = -INFINITY, my_lse = -INFINITY;
@@ -160,6 +258,7 @@ __global__ void __launch_bounds__(kMuThreads, 1)
             *reinterpret_cast<__nv_bfloat16*>(sB + sw128_elem(j, f, kMuReqs)) = __float2bfloat16_rn(acc[q] * inv);
         }
       }
+      }
     }
   }
   fence_proxy_async_smem();   // the operand's generic-proxy stores, before the tensor core reads them
@@ -208,25 +307,40 @@ __global__ void __launch_bounds__(kMuThreads, 1)
   const bool done =
       warp < 4 && __all_sync(0xffffffffu, mbar_wait_bounded(&bars[uDone], 0, p.err, kErrTimeoutEpilogue));
   tc_fence_after();
+  __shared__ int staged;
+  if (threadIdx.x == 0) staged = 0;
   if (done && !*abort_flag) {
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem);   // [32 requests][256 channels], over stage 0
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint32_t r[32];
       tmem_ld32(tmem + lane_base + 32 * half, r);
       tmem_ld_wait();
       const int ch = 128 * half + 32 * warp + lane;
+      if (p.vec_out) {
 #pragma unroll
-      for (int j = 0; j < kMuReqs; ++j) {
-        const int b = b0 + j;
-        if (b < p.num_reqs)
-          p.out[static_cast<long long>(b) * p.sot + static_cast<long long>(h) * p.soh + ch] =
-              __float2bfloat16_rn(__uint_as_float(r[j]));
+        for (int j = 0; j < kMuReqs; ++j) stg[j * kD + ch] = __float2bfloat16_rn(__uint_as_float(r[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < kMuReqs; ++j) {
+          const int b = b0 + j;
+          if (b < p.num_reqs)
+            p.out[static_cast<long long>(b) * p.sot + static_cast<long long>(h) * p.soh + ch] =
+                __float2bfloat16_rn(__uint_as_float(r[j]));
+        }
       }
     }
+    if (threadIdx.x == 0) staged = p.vec_out;
   }
   tc_fence_before();
   __syncthreads();
+  if (staged) {   // request j = warp, 8 channels a lane: one 512-byte row a warp
+    const int b = b0 + warp;
+    if (b < p.num_reqs)
+      *reinterpret_cast<uint4*>(p.out + static_cast<long long>(b) * p.sot + static_cast<long long>(h) * p.soh +
+                                8 * lane) = reinterpret_cast<const uint4*>(smem)[warp * (kD / 8) + lane];
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 64);

@@ -197,6 +197,15 @@ def merge_segments(part: torch.Tensor, sched: DecodeSchedule, out: torch.Tensor,
     torch.ops.lrkv_b200.merge_segments(part, sched.seg_base, out, lse)
 
 
+def partial_buffer(rows: int, r_v: int, device) -> torch.Tensor:
+    """Partial outputs for ``latent_decode`` / ``merge_segments`` / ``merge_up_project``: fp32 [rows, H, r_v + 1]
+    (the r_v normalised features and the natural-log LSE of every segment and head), allocated with the head stride
+    rounded up to a multiple of 4 floats so that every row starts on 16 bytes (the fused merge then reads the rows as
+    float4). A view of that allocation; any other [rows, H, r_v + 1] layout with a contiguous last dim works as well."""
+    width = (r_v + 1 + 3) // 4 * 4
+    return torch.empty(rows, H, width, dtype=torch.float32, device=device)[:, :, :r_v + 1]
+
+
 def merge_up_project(part: torch.Tensor, sched: DecodeSchedule, v_up_t: torch.Tensor, out: torch.Tensor,
                      lse: torch.Tensor) -> None:
     """``merge_segments`` and the V up-projection in one kernel: part [segments, H, lv + 1] -> out [B, H, 256] (BF16,

@@ -318,8 +318,7 @@ class LatentAttentionImpl:
             if side is not None:
                 torch.cuda.current_stream(dev).wait_stream(side)   # the step's own rows are part of the context
                 side = None
-            part = torch.empty(nd + m.sched.num_ctas, self.num_heads, lat.v_rank + 1, dtype=torch.float32,
-                               device=dev)
+            part = dec.partial_buffer(nd + m.sched.num_ctas, lat.v_rank, dev)
             lse = torch.empty(nd, self.num_heads, dtype=torch.float32, device=dev)
             dec.latent_decode(q_bd, cache, m.block_table[:nd], m.seq_lens[:nd], m.sched, part, self.scale,
                               lat.v_offset, lat.v_rank, rope=lat.rope)

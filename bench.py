@@ -166,7 +166,8 @@ class Workload:
         self.slots = (bt[torch.arange(self.B), pos // page].long() * page + pos % page).to(device)
         self.sched = dec.make_schedule(self.B, device)
         self.side = torch.cuda.Stream(device)
-        self.part = torch.empty(self.B + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
+        # head stride 644: every partial row starts on 16 bytes (float4 loads in the fused merge)
+        self.part = torch.empty(self.B + self.sched.num_ctas, H, 644, dtype=torch.float32, device=device)
         self.lse = torch.empty(self.B, H, dtype=torch.float32, device=device)
         self.out = torch.empty(self.L, self.B, H, D, dtype=torch.bfloat16, device=device)
 
@@ -791,7 +792,7 @@ class ServingRun:
         self.x = torch.randn(self.L, Bmax, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
         self.xp = torch.randn(4, chunk, self.hidden, generator=gq, device=device, dtype=torch.bfloat16)
         self.sched = dec.make_schedule(Bmax, device)
-        self.part = torch.empty(Bmax + self.sched.num_ctas, H, 641, dtype=torch.float32, device=device)
+        self.part = torch.empty(Bmax + self.sched.num_ctas, H, 644, dtype=torch.float32, device=device)
         self.lse = torch.empty(Bmax, H, dtype=torch.float32, device=device)
         self.out = torch.empty(self.L, Bmax, H, D, dtype=torch.bfloat16, device=device)
         self.side = torch.cuda.Stream(device)

@@ -359,6 +359,13 @@ def test_merge_up_project():
         out = torch.full((B, 24, 256), float("nan"), dtype=torch.bfloat16, device=DEV)
         lse = torch.full((B, 24), float("nan"), device=DEV)
         dec.merge_up_project(part_d, sched, v_d, out, lse)
+        # the same partials with 16-byte aligned rows (the backend's layout: float4 loads of the rows where lv % 4 == 0),
+        # into an output whose head stride is not a multiple of 8 (element stores instead of the staged 16-byte ones)
+        part_p = dec.partial_buffer(nseg + 1, lv, DEV)
+        part_p.copy_(part_d)
+        out_p = torch.full((B, 24, 260), float("nan"), dtype=torch.bfloat16, device=DEV)[:, :, :256]
+        lse_p = torch.full((B, 24), float("nan"), device=DEV)
+        dec.merge_up_project(part_p, sched, v_d, out_p, lse_p)
         a2 = torch.empty(B, 24, lv, dtype=torch.bfloat16, device=DEV)
         lse2 = torch.empty(B, 24, device=DEV)
         dec.merge_segments(part_d, sched, a2, lse2)
@@ -368,6 +375,7 @@ def test_merge_up_project():
         dec.check_device_errors(DEV)
         what = f"{B} requests, {nct} CTAs, lv {lv}"
         assert bf16_ulp_close(out.cpu(), out2.cpu(), ulps=1, atol=1e-5), what
+        assert torch.equal(out_p.cpu(), out.cpu()) and torch.equal(lse_p.cpu(), lse.cpu()), what + " (aligned rows)"
         assert torch.equal(torch.isinf(lse.cpu()), torch.isinf(lse2.cpu())), what
         live = torch.isfinite(lse2.cpu())
         assert torch.allclose(lse.cpu()[live], lse2.cpu()[live], atol=1e-6, rtol=0), what
