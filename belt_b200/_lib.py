@@ -18,6 +18,8 @@ c_i32p = ctypes.POINTER(ctypes.c_int32)
 SIGNATURES = {
     "belt_decode_schedule": [c_vp, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
     "belt_decode_schedule_weighted": [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
+    "belt_decode_schedule_balanced": [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
+                                      c_vp, c_vp],
     "belt_block_diag_query": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_i32p, c_vp, c_vp, c_vp],
     "belt_up_project": [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp],
     "belt_latent_rows_to_cache": [c_vp, c_i64, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp,
@@ -27,6 +29,9 @@ SIGNATURES = {
     "belt_latent_decode": [c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp,
                            c_vp, c_i32, c_vp, c_i64, c_i64, c_f32, c_i32, c_i32, c_i32p, c_vp, c_i32, c_vp, c_i32,
                            c_vp, c_vp],
+    "belt_latent_decode_timed": [c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp,
+                                 c_vp, c_i32, c_vp, c_i64, c_i64, c_f32, c_i32, c_i32, c_i32p, c_vp, c_i32, c_vp,
+                                 c_i32, c_vp, c_vp, c_vp],
     "belt_merge_segments": [c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_vp, c_i64, c_i64, c_vp, c_i64, c_vp],
     "belt_latent_decode_noalloc": [c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_i32, c_i64, c_i64, c_vp, c_i64, c_vp,
                                    c_i32, c_i32, c_f32, c_i32, c_i32, c_i32p, c_vp, c_i32, c_vp, c_i32, c_vp, c_i64,

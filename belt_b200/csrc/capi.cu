@@ -139,7 +139,7 @@ extern "C" {
 
 const char* belt_last_error(void) { return g_last_error.c_str(); }
 
-int belt_abi_version(void) { return 201; }
+int belt_abi_version(void) { return 202; }
 
 int belt_path_counts(int64_t* counts, int32_t n) {
   if (!counts || n < 0) return fail(BELT_ERR_INVALID, "path_counts: null buffer");
@@ -182,6 +182,24 @@ int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int
                 (long long)work_capacity, (long long)num_reqs + num_ctas);
   belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, 8, start_cost, work,
                          work_capacity, cta_seg, seg_base, err};
+  cudaError_t e = belt::launch_schedule(p, as_stream(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "schedule launch");
+}
+
+int belt_decode_schedule_balanced(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                                  int32_t start_cost, int64_t* cta_ns, float* cta_weight, int64_t* cta_cap,
+                                  int32_t* work, int64_t work_capacity, int32_t* cta_seg, int32_t* seg_base,
+                                  int32_t* err, void* stream) {
+  if (num_reqs < 0 || num_ctas < 1) return fail(BELT_ERR_INVALID, "schedule: num_reqs %d, num_ctas %d", num_reqs, num_ctas);
+  if (start_cost < 0 || start_cost > 1024) return fail(BELT_ERR_INVALID, "schedule: start_cost %d outside [0, 1024]", start_cost);
+  if ((num_reqs > 0 && !seq_lens) || !work || !cta_seg || !seg_base || !cta_ns || !cta_weight || !cta_cap)
+    return fail(BELT_ERR_INVALID, "schedule: null buffer");
+  if (work_capacity < static_cast<int64_t>(num_reqs) + num_ctas)
+    return fail(BELT_ERR_INVALID, "schedule: work capacity %lld < num_reqs + num_ctas = %lld",
+                (long long)work_capacity, (long long)num_reqs + num_ctas);
+  belt::ScheduleParams p{seq_lens, num_reqs, num_ctas, min_tiles, BELT_DECODE_TILE, 8, start_cost, work,
+                         work_capacity, cta_seg, seg_base, err, reinterpret_cast<long long*>(cta_ns), cta_weight,
+                         reinterpret_cast<long long*>(cta_cap)};
   cudaError_t e = belt::launch_schedule(p, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "schedule launch");
 }
@@ -429,13 +447,14 @@ int belt_latent_proj_rows_to_cache(const void* x, int64_t num_tokens, int64_t x_
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_proj_rows_to_cache launch");
 }
 
-int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+namespace {
+int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
                        int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
                        const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* work,
                        const int32_t* cta_seg, int32_t num_ctas, float* part, int64_t part_ss, int64_t part_sh,
                        float sm_scale, int32_t lk_pad, int32_t lv, const int32_t* rope_groups,
                        const void* rope_blocks, int32_t n_rope_blocks, const void* cos_sin, int32_t max_pos,
-                       int32_t* err, void* stream) {
+                       int32_t* err, int64_t* cta_ns, void* stream) {
   using namespace belt;
   if (num_reqs < 0 || num_ctas < 1) return fail(BELT_ERR_INVALID, "latent_decode: num_reqs %d, num_ctas %d", num_reqs, num_ctas);
   if (num_reqs == 0) return ok();
@@ -474,6 +493,7 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   p.part_ss = part_ss;
   p.part_sh = part_sh;
   p.err = err;
+  p.cta_ns = reinterpret_cast<unsigned long long*>(cta_ns);
   p.num_reqs = num_reqs;
   p.num_blocks = static_cast<int>(num_blocks);
   p.page = page;
@@ -618,6 +638,32 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   }
   cudaError_t e = launch_latent_decode(maps, p, num_ctas, as_stream(stream));
   return e == cudaSuccess ? ok() : cuda_fail(e, "latent_decode launch");
+}
+}  // namespace
+
+int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                       int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                       const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* work,
+                       const int32_t* cta_seg, int32_t num_ctas, float* part, int64_t part_ss, int64_t part_sh,
+                       float sm_scale, int32_t lk_pad, int32_t lv, const int32_t* rope_groups,
+                       const void* rope_blocks, int32_t n_rope_blocks, const void* cos_sin, int32_t max_pos,
+                       int32_t* err, void* stream) {
+  return latent_decode_impl(q_bd, num_reqs, kq, cache, num_blocks, page, row_width, stride_block, stride_tok,
+                            block_table, bt_stride, seq_lens, work, cta_seg, num_ctas, part, part_ss, part_sh, sm_scale,
+                            lk_pad, lv, rope_groups, rope_blocks, n_rope_blocks, cos_sin, max_pos, err, nullptr, stream);
+}
+
+int belt_latent_decode_timed(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                             int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                             const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                             const int32_t* work, const int32_t* cta_seg, int32_t num_ctas, float* part,
+                             int64_t part_ss, int64_t part_sh, float sm_scale, int32_t lk_pad, int32_t lv,
+                             const int32_t* rope_groups, const void* rope_blocks, int32_t n_rope_blocks,
+                             const void* cos_sin, int32_t max_pos, int32_t* err, int64_t* cta_ns, void* stream) {
+  if (!cta_ns) return fail(BELT_ERR_INVALID, "latent_decode_timed: null cta_ns");
+  return latent_decode_impl(q_bd, num_reqs, kq, cache, num_blocks, page, row_width, stride_block, stride_tok,
+                            block_table, bt_stride, seq_lens, work, cta_seg, num_ctas, part, part_ss, part_sh, sm_scale,
+                            lk_pad, lv, rope_groups, rope_blocks, n_rope_blocks, cos_sin, max_pos, err, cta_ns, stream);
 }
 
 }  // extern "C"

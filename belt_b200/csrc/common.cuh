@@ -338,6 +338,13 @@ __device__ __forceinline__ void warpgroup_reg_dealloc() {
 // stream has finished; grid_dependency_wait() blocks the calling thread until that kernel has completed and its
 // memory is visible (it returns at once when there is no such kernel). allow_dependents_launch() lets the next
 // kernel, if launched that way, start launching now.
+// The GPU's nanosecond clock (the same on every SM).
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 

@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bars);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  unsigned long long* t_begin = reinterpret_cast<unsigned long long*>(tmem_slot + 2);   // the CTA's start (cta_ns)
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -497,6 +498,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       // the query comes from the kernel ahead of this one (the absorbed-query GEMM), which may still be running; every
       // global write of this kernel (the partials) comes after the query, so after this wait as well
       grid_dependency_wait();
+      if (lane == 0) *t_begin = global_ns();
       int qsegs = 0;
       TileCursor c;
       c.begin(p, seg_begin, seg_end);
@@ -789,6 +791,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  // the CTA's time from its predecessor's completion to here, for the next step's balanced split
+  if (threadIdx.x == 0 && p.cta_ns && has_work && !*abort_flag) atomicAdd(p.cta_ns + blockIdx.x, global_ns() - *t_begin);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -25,6 +25,7 @@ struct DecodeParams {
   float* part;
   long long part_ss, part_sh;
   int* err;
+  unsigned long long* cta_ns;         // may be null: per CTA, += ns from the predecessor's completion to the CTA's exit
   int num_reqs;
   int num_blocks, page;
   // cache stages: a stage holds `cps` 64-column chunks of 128 tokens. Chunked layout (4-D boxes of 8 rows x nch
@@ -103,6 +104,11 @@ struct ScheduleParams {
   int32_t* cta_seg;
   int32_t* seg_base;
   int* err;
+  // balanced split (all three or none): per CTA the decode time of the previous step (read, then zeroed), its speed
+  // weight (updated in place) and the cost it was dealt (written)
+  long long* cta_ns;
+  float* cta_w;
+  long long* cta_cap;
 };
 cudaError_t launch_schedule(const ScheduleParams& p, cudaStream_t stream);
 

@@ -9,6 +9,10 @@
 //   work[k]     = (request, first tile, end tile, 0), segments in request order;
 //   seg_base[b] = first segment of request b, seg_base[B] = number of segments;
 //   cta_seg[c]  = first segment of CTA c, cta_seg[num_ctas] = number of segments.
+// Balanced split (cta_w given): the CTAs' shares of the cost follow per-CTA speed weights learned from the decode
+// launches' measured times (cta_ns / cta_cap of the previous step), so that CTAs on slower SMs get less work:
+// CTA c covers the costs [B_c, B_(c+1)) with B_c = per * num_ctas * W_c / W (W_c the weights' prefix sum), which is
+// c * per when every weight is equal.
 // One CTA of 1024 threads; requests are processed in chunks of 1024 with block-wide exclusive scans.
 #include "common.cuh"
 #include "launch.h"
@@ -17,6 +21,7 @@ namespace belt {
 
 namespace {
 constexpr int kSchedThreads = 1024;
+constexpr int kMaxBalancedCtas = 1024;
 
 // Block-wide exclusive scan of one value per thread; returns this thread's prefix and writes the total.
 __device__ long long block_exclusive_scan(long long v, long long* warp_sums, long long* total) {
@@ -49,6 +54,7 @@ __device__ long long block_exclusive_scan(long long v, long long* warp_sums, lon
 __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleParams p) {
   __shared__ long long warp_sums[32];
   __shared__ long long total_s;
+  __shared__ long long bounds[kMaxBalancedCtas + 1];   // balanced split: first cost of every CTA
   const int B = p.num_reqs;
   const int tile = p.tile;
   const long long u = p.unit, s0 = p.start_cost;
@@ -68,6 +74,59 @@ __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleP
   per = per > u * p.min_tiles ? per : u * p.min_tiles;
   per = per > u ? per : u;
   auto cdiv = [](long long a, long long b) { return a >= 0 ? (a + b - 1) / b : -((-a) / b); };
+  // balanced split: learn the weights from the previous step's times, then the CTAs' cost bounds
+  const bool tuned = p.cta_w != nullptr;
+  const bool balanced = tuned && per >= 8 * u && p.num_ctas <= kMaxBalancedCtas;
+  if (tuned) {
+    const int c = threadIdx.x;
+    const bool mine = c < p.num_ctas;   // num_ctas <= 1024 whenever balanced
+    float w = 1.f;
+    double rate = 0.0;
+    bool seen = true;
+    if (balanced && mine) {
+      w = p.cta_w[c];
+      const long long ns = p.cta_ns[c], cap = p.cta_cap[c];
+      seen = ns > 0 && cap > 0;
+      rate = seen ? static_cast<double>(cap) / static_cast<double>(ns) : 0.0;
+    }
+    if (balanced && __syncthreads_and(seen ? 1 : 0)) {
+      // mean rate over the CTAs (a fixed-point sum keeps the block scan integral and the result deterministic)
+      const long long rq = mine ? static_cast<long long>(rate * 1e9) : 0;   // cost units per second
+      block_exclusive_scan(rq, warp_sums, &total_s);
+      const double mean = static_cast<double>(total_s) / p.num_ctas;
+      if (mine && mean > 0.0) {
+        const float r = static_cast<float>(static_cast<double>(rq) / mean);
+        w = fminf(fmaxf(0.5f * w + 0.5f * r, 0.8f), 1.25f);
+      }
+    }
+    if (balanced) {
+      // normalise to mean 1 in fixed point (2^20 per unit weight), then the prefix sums give the bounds
+      const long long wq = mine ? static_cast<long long>(w * 1048576.f + 0.5f) : 0;
+      const long long before = block_exclusive_scan(wq, warp_sums, &total_s);
+      const long long span = per * p.num_ctas, wsum = total_s;
+      if (mine) {
+        bounds[c] = span * before / wsum;
+        p.cta_w[c] = static_cast<float>(static_cast<double>(wq) * p.num_ctas / static_cast<double>(wsum));
+      }
+      if (c == 0) bounds[p.num_ctas] = span;
+      __syncthreads();
+    }
+    for (int k = threadIdx.x; k < p.num_ctas; k += kSchedThreads) {
+      p.cta_cap[k] = balanced ? bounds[k + 1] - bounds[k] : per;
+      p.cta_ns[k] = 0;
+    }
+  }
+  // first cost of CTA c, and the CTA holding cost x (the last c with lo(c) <= x)
+  auto lo = [&](long long c) -> long long { return balanced ? bounds[c] : c * per; };
+  auto cta_of = [&](long long x) -> long long {
+    if (!balanced) return x / per;
+    int a = 0, b = p.num_ctas;   // bounds[a] <= x < bounds[b]
+    while (b - a > 1) {
+      const int m = (a + b) >> 1;
+      if (bounds[m] <= x) a = m; else b = m;
+    }
+    return a;
+  };
   // pass 2: segments. Tile k of request b starts at cost x_b + s0 + u k (x_b: the request's cost offset) and belongs
   // to CTA floor(cost / per); consecutive tiles of one request on one CTA form a segment.
   long long seg_carry = 0;
@@ -78,8 +137,8 @@ __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleP
       tiles = (static_cast<long long>(p.seq_lens[b]) + tile - 1) / tile;
       x = p.seg_base[b];
       if (tiles > 0) {
-        c0 = (x + s0) / per;
-        nseg = (x + s0 + u * (tiles - 1)) / per - c0 + 1;
+        c0 = cta_of(x + s0);
+        nseg = cta_of(x + s0 + u * (tiles - 1)) - c0 + 1;
       }
     }
     const long long base = seg_carry + block_exclusive_scan(nseg, warp_sums, &total_s);
@@ -87,12 +146,12 @@ __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleP
       p.seg_base[b] = static_cast<int32_t>(base);
       if (nseg > 0) {
         // CTAs after the previous request's last tile up to this one's first start at this request's first segment
-        const long long prev = x > 0 ? (x - u) / per : -1;
+        const long long prev = x > 0 ? cta_of(x - u) : -1;
         for (long long c = prev + 1; c <= c0 && c <= p.num_ctas; ++c) p.cta_seg[c] = static_cast<int32_t>(base);
       }
       for (long long j = 0; j < nseg; ++j) {
         const long long cta = c0 + j;
-        long long k0 = cdiv(cta * per - x - s0, u), k1 = cdiv((cta + 1) * per - x - s0, u);
+        long long k0 = cdiv(lo(cta) - x - s0, u), k1 = cdiv(lo(cta + 1) - x - s0, u);
         k0 = k0 > 0 ? k0 : 0;
         k1 = k1 < tiles ? k1 : tiles;
         const long long k = base + j;
@@ -112,7 +171,7 @@ __global__ void __launch_bounds__(kSchedThreads) schedule_kernel(const ScheduleP
   }
   if (threadIdx.x == 0) p.seg_base[B] = static_cast<int32_t>(seg_carry);
   // CTAs after the last tile (and every CTA when there are no tiles) start at the end
-  const long long last = total_cost > 0 ? (total_cost - u) / per : -1;
+  const long long last = total_cost > 0 ? cta_of(total_cost - u) : -1;
   for (long long c = last + 1 + threadIdx.x; c <= p.num_ctas; c += kSchedThreads)
     p.cta_seg[c] = static_cast<int32_t>(seg_carry);
 }

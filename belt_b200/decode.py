@@ -12,6 +12,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 import math
+import os
 
 import torch
 
@@ -69,6 +70,11 @@ class DecodeSchedule:
     # 0: the reference's split (equal runs of tiles); > 0: equal runs of cost, a tile costing 8 and a request's first
     # tile this much more (belt_decode_schedule_weighted)
     start_cost: int = 0
+    # balanced split (belt_decode_schedule_balanced; None: off): per CTA the decode time of the step so far (int64 ns,
+    # added by the decode launches), its speed weight (fp32) and the cost it was dealt (int64)
+    cta_ns: torch.Tensor | None = None
+    cta_w: torch.Tensor | None = None
+    cta_cap: torch.Tensor | None = None
 
     @property
     def capacity(self) -> int:
@@ -76,20 +82,32 @@ class DecodeSchedule:
 
 
 # Extra cost of a request's first tile in the weighted split, in eighths of a tile: a segment switch costs the decode
-# kernel a query reload and a partial-output epilogue, measured at about one tile's time.
-SCHEDULE_START_COST = 10
+# kernel a query reload and a partial-output epilogue, measured at 11.9 us against 7.4 us per tile (1.6 tiles).
+SCHEDULE_START_COST = 13
+# Balanced split by default (BELT_B200_BALANCE=0 turns it off): the CTAs' shares follow their measured speed, so the
+# split of a step depends on the times of the step before (outputs then differ between runs at the rounding level).
+SCHEDULE_BALANCE = os.environ.get("BELT_B200_BALANCE", "1") != "0"
 
 
-def make_schedule(max_reqs: int, device, num_ctas: int | None = None,
-                  start_cost: int = SCHEDULE_START_COST) -> DecodeSchedule:
+def make_schedule(max_reqs: int, device, num_ctas: int | None = None, start_cost: int = SCHEDULE_START_COST,
+                  balance: bool | None = None) -> DecodeSchedule:
     """Buffers for up to ``max_reqs`` decode requests; one CTA per SM by default (cute_decode.py:562-568).
-    ``start_cost`` 0 keeps the reference's split; the default weights request starts (``DecodeSchedule``)."""
+    ``start_cost`` 0 keeps the reference's split; the default weights request starts (``DecodeSchedule``).
+    ``balance`` (default ``SCHEDULE_BALANCE``, only with ``start_cost`` > 0) deals the cost out by the CTAs' measured
+    speed: the decode launches time every CTA, the next ``schedule`` call updates the weights."""
     device = torch.device(device)
     if num_ctas is None:
         num_ctas = torch.cuda.get_device_properties(device).multi_processor_count
+    if balance is None:
+        balance = SCHEDULE_BALANCE
     i32 = dict(device=device, dtype=torch.int32)
-    return DecodeSchedule(num_ctas, torch.zeros(max_reqs + num_ctas, 4, **i32), torch.zeros(num_ctas + 1, **i32),
-                          torch.zeros(max_reqs + 1, **i32), int(start_cost))
+    sched = DecodeSchedule(num_ctas, torch.zeros(max_reqs + num_ctas, 4, **i32), torch.zeros(num_ctas + 1, **i32),
+                           torch.zeros(max_reqs + 1, **i32), int(start_cost))
+    if balance and start_cost > 0:
+        sched.cta_ns = torch.zeros(num_ctas, dtype=torch.int64, device=device)
+        sched.cta_w = torch.ones(num_ctas, dtype=torch.float32, device=device)
+        sched.cta_cap = torch.zeros(num_ctas, dtype=torch.int64, device=device)
+    return sched
 
 
 def schedule(sched: DecodeSchedule, seq_lens: torch.Tensor, min_tiles: int = 1) -> None:
@@ -101,8 +119,13 @@ def schedule(sched: DecodeSchedule, seq_lens: torch.Tensor, min_tiles: int = 1) 
         raise ValueError(f"schedule: {B} requests exceed the schedule's capacity {sched.seg_base.shape[0] - 1}")
     if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
         raise ValueError("schedule: seq_lens must be contiguous int32")
-    torch.ops.lrkv_b200.decode_schedule(seq_lens, sched.work, sched.cta_seg, sched.seg_base, sched.num_ctas,
-                                        int(min_tiles), int(sched.start_cost))
+    if sched.cta_w is not None:
+        torch.ops.lrkv_b200.decode_schedule_balanced(seq_lens, sched.work, sched.cta_seg, sched.seg_base, sched.cta_ns,
+                                                     sched.cta_w, sched.cta_cap, sched.num_ctas, int(min_tiles),
+                                                     int(sched.start_cost))
+    else:
+        torch.ops.lrkv_b200.decode_schedule(seq_lens, sched.work, sched.cta_seg, sched.seg_base, sched.num_ctas,
+                                            int(min_tiles), int(sched.start_cost))
 
 
 def block_diag_query(q_lat: torch.Tensor, q_rot: torch.Tensor, k_off: list, k_ranks: list, lk_pad: int,
@@ -179,8 +202,14 @@ def latent_decode(q_bd: torch.Tensor, cache: torch.Tensor, block_table: torch.Te
     if cos_sin.dtype != torch.bfloat16 or not cos_sin.is_contiguous() or cos_sin.shape[1] != ROT:
         raise ValueError("cos_sin must be contiguous BF16 [max_pos, 64]")
     groups = [int(x) for gr in rope.groups for x in gr]
-    torch.ops.lrkv_b200.latent_decode(q_bd, cache, block_table, seq_lens, sched.work, sched.cta_seg, part,
-                                      sched.num_ctas, float(sm_scale), int(lk_pad), int(lv), groups, blocks, cos_sin)
+    if sched.cta_ns is not None:   # balanced split: time every CTA for the next step's weights
+        torch.ops.lrkv_b200.latent_decode_timed(q_bd, cache, block_table, seq_lens, sched.work, sched.cta_seg, part,
+                                                sched.num_ctas, float(sm_scale), int(lk_pad), int(lv), groups, blocks,
+                                                cos_sin, sched.cta_ns)
+    else:
+        torch.ops.lrkv_b200.latent_decode(q_bd, cache, block_table, seq_lens, sched.work, sched.cta_seg, part,
+                                          sched.num_ctas, float(sm_scale), int(lk_pad), int(lv), groups, blocks,
+                                          cos_sin)
 
 
 latent_decode_cute = latent_decode   # the reference's name for the same entry

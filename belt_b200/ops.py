@@ -17,8 +17,11 @@ Operators (mutated arguments marked !):
   cache_write(c, slot_mapping, cache!, u_cat, k_segs, eps)
   proj_cache_write(x, w_down, slot_mapping, cache!, u_cat, k_segs, eps)
   decode_schedule(seq_lens, work!, cta_seg!, seg_base!, num_ctas, min_tiles, start_cost)
+  decode_schedule_balanced(seq_lens, work!, cta_seg!, seg_base!, cta_ns!, cta_w!, cta_cap!, num_ctas, min_tiles,
+                           start_cost)
   latent_decode(q_bd, cache, block_table, seq_lens, work, cta_seg, part!, num_ctas, sm_scale, lk_pad, lv,
                 rope_groups, rope_blocks, cos_sin)
+  latent_decode_timed(..., as latent_decode, cta_ns!)
   merge_segments(part, seg_base, out!, lse!)
   merge_up_project(part, seg_base, v_up_t, out!, lse!)
   block_diag_query(q, qmap, col_runs) -> q_bd
@@ -106,6 +109,21 @@ def _(seq_lens, work, cta_seg, seg_base, num_ctas, min_tiles, start_cost):
     return None
 
 
+@custom_op(f"{NS}::decode_schedule_balanced", mutates_args=("work", "cta_seg", "seg_base", "cta_ns", "cta_w", "cta_cap"),
+           device_types="cuda")
+def decode_schedule_balanced(seq_lens: torch.Tensor, work: torch.Tensor, cta_seg: torch.Tensor, seg_base: torch.Tensor,
+                             cta_ns: torch.Tensor, cta_w: torch.Tensor, cta_cap: torch.Tensor, num_ctas: int,
+                             min_tiles: int, start_cost: int) -> None:
+    _lib.call("belt_decode_schedule_balanced", seq_lens.data_ptr(), seq_lens.shape[0], num_ctas, min_tiles, start_cost,
+              cta_ns.data_ptr(), cta_w.data_ptr(), cta_cap.data_ptr(), work.data_ptr(), work.shape[0],
+              cta_seg.data_ptr(), seg_base.data_ptr(), _err(seq_lens), _stream(seq_lens))
+
+
+@decode_schedule_balanced.register_fake
+def _(seq_lens, work, cta_seg, seg_base, cta_ns, cta_w, cta_cap, num_ctas, min_tiles, start_cost):
+    return None
+
+
 @custom_op(f"{NS}::latent_decode", mutates_args=("part",), device_types="cuda")
 def latent_decode(q_bd: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
                   work: torch.Tensor, cta_seg: torch.Tensor, part: torch.Tensor, num_ctas: int, sm_scale: float,
@@ -123,6 +141,26 @@ def latent_decode(q_bd: torch.Tensor, cache: torch.Tensor, block_table: torch.Te
 @latent_decode.register_fake
 def _(q_bd, cache, block_table, seq_lens, work, cta_seg, part, num_ctas, sm_scale, lk_pad, lv, rope_groups,
       rope_blocks, cos_sin):
+    return None
+
+
+@custom_op(f"{NS}::latent_decode_timed", mutates_args=("part", "cta_ns"), device_types="cuda")
+def latent_decode_timed(q_bd: torch.Tensor, cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
+                        work: torch.Tensor, cta_seg: torch.Tensor, part: torch.Tensor, num_ctas: int, sm_scale: float,
+                        lk_pad: int, lv: int, rope_groups: list[int], rope_blocks: torch.Tensor,
+                        cos_sin: torch.Tensor, cta_ns: torch.Tensor) -> None:
+    _aligned(cache)
+    _lib.call("belt_latent_decode_timed", q_bd.data_ptr(), q_bd.shape[0], q_bd.shape[2], cache.data_ptr(),
+              cache.shape[0], cache.shape[1], cache.shape[2], cache.stride(0), cache.stride(1), block_table.data_ptr(),
+              block_table.stride(0), seq_lens.data_ptr(), work.data_ptr(), cta_seg.data_ptr(), num_ctas,
+              part.data_ptr(), part.stride(0), part.stride(1), float(sm_scale), int(lk_pad), int(lv),
+              _lib.int_array(rope_groups), rope_blocks.data_ptr(), rope_blocks.shape[-1] // 64, cos_sin.data_ptr(),
+              cos_sin.shape[0], _err(q_bd), cta_ns.data_ptr(), _stream(q_bd))
+
+
+@latent_decode_timed.register_fake
+def _(q_bd, cache, block_table, seq_lens, work, cta_seg, part, num_ctas, sm_scale, lk_pad, lv, rope_groups,
+      rope_blocks, cos_sin, cta_ns):
     return None
 
 
@@ -271,7 +309,8 @@ def _(x, weight):
     return x.new_empty(x.shape[0], weight.shape[0])
 
 
-OPS = ("cache_write", "proj_cache_write", "decode_schedule", "latent_decode", "merge_segments", "merge_up_project",
+OPS = ("cache_write", "proj_cache_write", "decode_schedule", "decode_schedule_balanced", "latent_decode",
+       "latent_decode_timed", "merge_segments", "merge_up_project",
        "block_diag_query",
        "up_project", "decompress", "prefill_attention", "decompress_varlen", "prefill_attention_varlen", "attn_fold",
        "linear")

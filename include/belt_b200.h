@@ -30,7 +30,7 @@ extern "C" {
 const char* belt_last_error(void);
 
 /* ABI version of this library (major * 100 + minor). 200: the per-head GEMM entry points take an error word;
- * 201: belt_path_counts. */
+ * 201: belt_path_counts; 202: belt_decode_schedule_balanced, belt_latent_decode_timed. */
 int belt_abi_version(void);
 
 /*
@@ -64,6 +64,24 @@ int belt_decode_schedule(const int32_t* seq_lens, int32_t num_reqs, int32_t num_
 int belt_decode_schedule_weighted(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
                                   int32_t start_cost, int32_t* work, int64_t work_capacity, int32_t* cta_seg,
                                   int32_t* seg_base, int32_t* err, void* stream);
+
+/*
+ * The weighted split dealt out by measured CTA speed (no reference counterpart; same outputs and capacities as
+ * belt_decode_schedule_weighted). cta_ns [num_ctas] int64: per CTA the nanoseconds its decode launches of the previous
+ * step took (belt_latent_decode_timed adds them; this call reads and zeroes them); cta_weight [num_ctas] fp32 (start
+ * at 1.0): per CTA speed weight, updated in place when every CTA has a time; cta_cap [num_ctas] int64 (written): the
+ * cost each CTA was dealt. The update: rate_c = cap_c / ns_c, w_c = clamp(0.5 w_c + 0.5 rate_c / mean(rate),
+ * 0.8, 1.25), then normalised to mean 1; CTA c gets the cost range [per * num_ctas * W_c / W, per * num_ctas *
+ * W_(c+1) / W) where W_c is the sum of the weights before c (exactly the weighted split when every weight is equal).
+ * CTAs on slower SMs get less work, so that the CTAs of a launch finish together. The weights are used only when
+ * every CTA gets at least 8 tiles' cost (and num_ctas <= 1024); otherwise this is the weighted split. The split then
+ * depends on measured times: two runs of the same step can cut segments at other tiles (results differ at the
+ * rounding level of the merge).
+ */
+int belt_decode_schedule_balanced(const int32_t* seq_lens, int32_t num_reqs, int32_t num_ctas, int32_t min_tiles,
+                                  int32_t start_cost, int64_t* cta_ns, float* cta_weight, int64_t* cta_cap,
+                                  int32_t* work, int64_t work_capacity, int32_t* cta_seg, int32_t* seg_base,
+                                  int32_t* err, void* stream);
 
 /*
  * Absorbed block-diagonal decode query: replaces latent_ops.py:67-73 (`block_diag_query`, the grouped GEMM of
@@ -140,6 +158,19 @@ int belt_latent_decode(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
                        float sm_scale, int32_t lk_pad, int32_t lv, const int32_t* rope_groups,
                        const void* rope_blocks, int32_t n_rope_blocks, const void* cos_sin, int32_t max_pos,
                        int32_t* err, void* stream);
+
+/*
+ * belt_latent_decode that also times every CTA (no reference counterpart): cta_ns [num_ctas] int64 (device), CTA c
+ * adds the nanoseconds from the completion of the kernel ahead of it in the stream (the absorbed query) to its exit.
+ * belt_decode_schedule_balanced reads them for the next step's split.
+ */
+int belt_latent_decode_timed(const void* q_bd, int32_t num_reqs, int32_t kq, const void* cache, int64_t num_blocks,
+                             int32_t page, int32_t row_width, int64_t stride_block, int64_t stride_tok,
+                             const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+                             const int32_t* work, const int32_t* cta_seg, int32_t num_ctas, float* part,
+                             int64_t part_ss, int64_t part_sh, float sm_scale, int32_t lk_pad, int32_t lv,
+                             const int32_t* rope_groups, const void* rope_blocks, int32_t n_rope_blocks,
+                             const void* cos_sin, int32_t max_pos, int32_t* err, int64_t* cta_ns, void* stream);
 
 /*
  * Segment merge: replaces cute_decode.py:715-722 (`merge_segments`, kernel `_merge_segments` :681-712).

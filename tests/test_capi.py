@@ -36,7 +36,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.belt_abi_version() == 201
+    assert lib.belt_abi_version() == 202
 
 
 def _decode_args(**over):

@@ -96,6 +96,87 @@ def test_schedule_weighted_bit_exact(seqs, nct, start_cost):
     assert torch.equal(sched.work[:total].cpu(), torch.from_numpy(work[:total]))
 
 
+def balanced_split(seqs, nct, start_cost, w, tile=128, unit=8):
+    """The balanced split restated tile by tile: CTA c takes the tiles whose cost position x_b + s0 + 8 k falls in
+    [B_c, B_(c+1)), B_c = per * nct * W_c // W with W_c the prefix sums of the fixed-point weights."""
+    import numpy as np
+    tiles = [(L + tile - 1) // tile for L in seqs]
+    cost = [start_cost + unit * t if t > 0 else 0 for t in tiles]
+    total = sum(cost)
+    per = max(-(-total // nct), unit, unit)
+    wq = [int(np.float32(np.float32(x) * np.float32(1048576.0) + np.float32(0.5))) for x in w]
+    pre = [0]
+    for q in wq:
+        pre.append(pre[-1] + q)
+    bounds = [per * nct * p // pre[-1] for p in pre]
+    owner = lambda pos: max(c for c in range(nct) if bounds[c] <= pos)
+    work, seg_base, seg_cta = [], [], []
+    x = 0
+    for b, t in enumerate(tiles):
+        seg_base.append(len(work))
+        prev = None
+        for k in range(t):
+            c = owner(x + start_cost + unit * k)
+            if c != prev:
+                work.append([b, k, k + 1, 0])
+                seg_cta.append(c)
+                prev = c
+            else:
+                work[-1][2] = k + 1
+        x += cost[b]
+    seg_base.append(len(work))
+    cta_seg = [next((i for i, c in enumerate(seg_cta) if c >= cc), len(work)) for cc in range(nct + 1)]
+    return work, cta_seg, seg_base, bounds, wq
+
+
+@pytest.mark.parametrize("seqs,nct", [([8192] * 64, 148), ([3000, 1, 1, 1, 7000, 64, 63, 65] * 20, 148),
+                                      ([200] * 300, 148), (list(range(1000, 60000, 997)), 100)])
+def test_schedule_balanced(seqs, nct):
+    """The balanced split: a fresh schedule is the weighted split; after a step whose CTAs ran at different speeds the
+    weights follow cap / ns (as belt_decode_schedule_balanced documents, in the same fp32 / fixed-point arithmetic),
+    the work follows the weights tile by tile, and the times are zeroed for the next step."""
+    import numpy as np
+    B, sc = len(seqs), dec.SCHEDULE_START_COST
+    sched = dec.make_schedule(B, DEV, num_ctas=nct, start_cost=sc, balance=True)
+    sl = torch.tensor(seqs, dtype=torch.int32, device=DEV)
+    dec.schedule(sched, sl)
+    work, cta_seg, seg_base = oracle.schedule_weighted(seqs, nct, dec.TILE_T, sc)
+    assert torch.equal(sched.cta_seg.cpu(), torch.from_numpy(cta_seg))
+    assert torch.equal(sched.work[:int(seg_base[-1])].cpu(), torch.from_numpy(work[:int(seg_base[-1])]))
+    for step in range(3):
+        cap = sched.cta_cap.cpu().double()
+        speed = 1.0 + 0.2 * torch.sin(torch.arange(nct, dtype=torch.float64) * (1.7 + step))
+        ns = (cap / speed * 1000.0).round().long()
+        sched.cta_ns.copy_(ns.to(DEV))
+        w_prev = sched.cta_w.cpu().numpy()
+        dec.schedule(sched, sl)
+        torch.cuda.synchronize()
+        tiles = [(L + dec.TILE_T - 1) // dec.TILE_T for L in seqs]
+        per = max(-(-sum(sc + 8 * t for t in tiles if t > 0) // nct), 8)
+        if per < 64:   # under 8 tiles a CTA the weights are not used: the weighted split, weights unchanged
+            assert torch.equal(sched.cta_seg.cpu(), torch.from_numpy(cta_seg)), step
+            assert np.array_equal(sched.cta_w.cpu().numpy(), w_prev) and not sched.cta_ns.cpu().any()
+            assert sched.cta_cap.cpu().tolist() == [per] * nct
+            continue
+        rq = [int(float(c) / float(n) * 1e9) for c, n in zip(cap.tolist(), ns.tolist())]
+        mean = sum(rq) / nct
+        f32 = np.float32
+        w = [min(max(f32(f32(0.5) * f32(wp) + f32(0.5) * f32(q / mean)), f32(0.8)), f32(1.25))
+             for wp, q in zip(w_prev, rq)]
+        ework, ecta, ebase, bounds, wq = balanced_split(seqs, nct, sc, w)
+        assert sched.seg_base[:B + 1].cpu().tolist() == ebase, step
+        assert sched.cta_seg.cpu().tolist() == ecta, step
+        assert sched.work[:ebase[-1]].cpu().tolist() == ework, step
+        assert sched.cta_cap.cpu().tolist() == [bounds[c + 1] - bounds[c] for c in range(nct)]
+        assert not sched.cta_ns.cpu().any()
+        got_w = sched.cta_w.cpu().numpy()
+        assert np.allclose(got_w, np.array(wq, dtype=np.float64) * nct / sum(wq), rtol=1e-6)
+        assert abs(got_w.mean() - 1.0) < 1e-5 and got_w.min() > 0.7 and got_w.max() < 1.4
+        # slower CTAs (higher ns per cost) get less: weights move with the speeds
+        if step == 0:
+            assert np.corrcoef(got_w, speed.numpy())[0, 1] > 0.9
+
+
 # ------------------------------------------------------------------------------------------------- cache write
 @pytest.mark.parametrize("name", CASES)
 @pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
