@@ -562,6 +562,25 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
         return fail(BELT_ERR_INVALID, "latent_decode: RoPE coordinates of group %d interleave with another group's", g);
     }
   }
+  // rebuild steps by key chunk: step ks = 4 cc + s of group g (ks0 <= ks <= ks1) reads image rope_e0[g] + ks - ks0
+  for (int cc = 0; cc < n_k; ++cc) {
+    unsigned long long v[2] = {0, 0};
+    for (int s16 = 0; s16 < 4; ++s16) {
+      const int ks = 4 * cc + s16;
+      int w = 0;
+      for (int g = 0; g < kG; ++g)
+        if (ks >= p.rope_ks0[g] && ks <= p.rope_ks1[g]) {
+          if (w == 2)
+            return fail(BELT_ERR_INVALID, "latent_decode: columns %d-%d hold RoPE coordinates of three groups", 16 * ks,
+                        16 * ks + 15);
+          const unsigned f = 0x8000u | (ks != p.rope_ks0[g] ? 0x4000u : 0u) |
+                             (static_cast<unsigned>(p.rope_e0[g] + ks - p.rope_ks0[g]) << 2) | static_cast<unsigned>(g);
+          v[w++] |= static_cast<unsigned long long>(f) << (16 * s16);
+        }
+    }
+    p.k_rebuild[cc][0] = v[0];
+    p.k_rebuild[cc][1] = v[1];
+  }
   for (int e = 0; e < nk; ++e) {
     p.kst_col[e] = ks_list[e].col;
     p.kst_src[e] = ks_list[e].src;
@@ -604,6 +623,7 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   }
   if (!planned)
     return fail(BELT_ERR_INVALID, "latent_decode: layout (n_k %d, %d rebuild steps) does not fit in shared memory", n_k, nk);
+  decode_plan_stages(p);
   const bool use_chunked = p.chunked != 0;
 
   DecodeMaps maps;

@@ -3,7 +3,7 @@
 // Replaces the reference's Hopper CuTe kernel ``LatentDecodeSm90`` (plugins/vllm_lrkv/vllm_lrkv/cute_decode.py:90-484)
 // with a Blackwell design. One CTA per SM walks the segments the schedule dealt it (cute_decode.py:571-598
 // semantics, 128-token tiles). Twelve warps in three warpgroups; warpgroup 0 gives registers to the other two
-// (setmaxnreg: 80 / 208 / 208 per thread, within the 3 x 168 the launch provides):
+// (setmaxnreg: 104 / 200 / 200 per thread, the 3 x 168 the launch provides):
 //
 // * warp 0, TMA producer (lanes 0-15, one box per lane and stage, issued in one instruction): streams the cache
 //   through a ring of stages, each `cps` 64-column chunks of 128 tokens, all SWIZZLE_128B. Two layouts:
@@ -11,8 +11,10 @@
 //       page (16 rows x 4 chunks = 8 KB at page 16), the 8-row groups landing as consecutive atoms of n KB;
 //     - page (any 8-aligned layout): 3-D boxes of `page` rows x 64 columns, 2 chunks per stage.
 //   Each lane reads its box's block id once per tile. Pages past the request are all-OOB boxes (zeros). Stage order is
-//   software-pipelined across tiles: K(0), K(1), V(0), K(2), V(1), ... so that tile i's softmax runs while tile i+1's
-//   key stages are scored and tile i's values stream in.
+//   software-pipelined across tiles: K(0), K(1) + V(0), K(2) + V(1), ... so that tile i's softmax runs while tile
+//   i+1's key chunks are scored and tile i's values stream in. One iteration's key and value chunks are packed into
+//   full stages (a stage may end one part and start the next: the host's stage plan, decode_plan_stages), so a row
+//   of 16 chunks takes 4 stages of 64 KB whatever its K / V split.
 // * warp 1, tcgen05 issuer (one thread; descriptors advance only their low words), M = 128 tokens:
 //     - scores S[tok, head] (N = 32: 24 heads; the last 8 columns are ignored) over the K part against the
 //       block-diagonal query;
@@ -48,7 +50,7 @@ constexpr int kQChunkBytes = 24 * 128;
 constexpr int kKstBytes = 64 * 16 * 2;          // [64 x 16] BF16 = 2 KB
 constexpr int kPBytes = kTile * 32 * 2;         // [128 tokens x 32 heads] BF16 = 8 KB
 constexpr int kThreads = 384;
-constexpr int kRegsWg0 = 80, kRegsWork = 208;   // 80 + 2 * 208 <= 3 * 168 registers per SMSP
+constexpr int kRegsWg0 = 104, kRegsWork = 200;   // 104 + 2 * 200 = 3 * 168 registers per SMSP
 constexpr int kProducerLanes = 16;             // one TMA box per lane and stage (16 boxes of a 128-token stage)
 constexpr int kTmemCols = 512;
 constexpr int kTmemK = 64;
@@ -74,6 +76,8 @@ constexpr int kNumBars = 32;
 static_assert(bImg < kNumBars, "barriers");
 // red_max [2][4][32], red_sum [4][32], flags [2][4], per-head alpha / 1 / sum [32]
 constexpr int kRedFloats = 2 * 4 * 32 + 4 * 32 + 2 * 4 + 32;
+constexpr int kKinfoBytes = 256;                // DecodeParams::k_rebuild, copied to shared memory at start
+static_assert(kKinfoBytes >= (kDecodeMaxQChunks - 4) * 16, "k_rebuild");
 }  // namespace dec
 
 bool decode_plan_smem(DecodeParams& p) {
@@ -81,7 +85,7 @@ bool decode_plan_smem(DecodeParams& p) {
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
   const int q_bytes = up((p.n_k + kG) * kQChunkBytes + 1024, 1024);
   const int b_bytes = p.n_kst * kKstBytes;
-  const int fixed = q_bytes + b_bytes + 2 * kPBytes + up(kRedFloats * 4, 128) + kNumBars * 8 + 16 + 1024;
+  const int fixed = q_bytes + b_bytes + 2 * kPBytes + up(kRedFloats * 4, 128) + kKinfoBytes + kNumBars * 8 + 16 + 1024;
   int stages = (kMaxSmem - fixed) / p.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
@@ -90,9 +94,50 @@ bool decode_plan_smem(DecodeParams& p) {
   p.off_b = p.off_q + q_bytes;
   p.off_p = p.off_b + b_bytes;
   p.off_red = p.off_p + 2 * kPBytes;
-  p.off_bars = p.off_red + up(kRedFloats * 4, 128);
+  p.off_kinfo = p.off_red + up(kRedFloats * 4, 128);
+  p.off_bars = p.off_kinfo + kKinfoBytes;
   p.smem_bytes = p.off_bars + kNumBars * 8 + 16 + 1024;
   return p.smem_bytes <= kMaxSmem;
+}
+
+void decode_plan_stages(DecodeParams& p) {
+  // Packed: the iteration's n_k key chunks and n_vc value chunks as one run cut every `cps` chunks. The value part
+  // starts at position n_k; its O^T blocks are chunk pairs starting at even positions (v_shift = n_k % 2), so a pair
+  // never spans two stages (cps is even). Separate (when a shifted value part would need more O^T blocks than TMEM
+  // holds): key stages, then value stages.
+  const int shift = p.n_k % 2;
+  const int n_vp = (p.n_vc + shift + 1) / 2;
+  p.packed = n_vp <= kDecodeMaxVPairs ? 1 : 0;
+  p.v_shift = p.packed ? shift : 0;
+  p.n_vp = (p.n_vc + p.v_shift + 1) / 2;
+  p.n_plan = p.packed ? (p.n_k + p.n_vc + p.cps - 1) / p.cps : p.n_ks + p.n_vs;
+}
+
+// Stage s of an iteration's plan: key chunks [k0, k0 + kn), value chunks [v0, v0 + vn) (an absent part has n = 0).
+// Closed-form arithmetic on scalar parameters: the MMA issuer runs it between two stages, and the tensor pipe idles
+// while that thread does anything but issue.
+struct StagePart {
+  int k0, kn, v0, vn;
+};
+
+__device__ __forceinline__ StagePart plan_stage(const DecodeParams& p, int s) {
+  StagePart r;
+  if (p.packed) {
+    const int lo = s * p.cps, hi = min(lo + p.cps, p.n_k + p.n_vc);
+    r.k0 = lo;
+    r.kn = max(min(hi, p.n_k) - lo, 0);
+    r.v0 = max(lo - p.n_k, 0);
+    r.vn = max(hi - max(lo, p.n_k), 0);
+  } else if (s < p.n_ks) {
+    r.k0 = p.cps * s;
+    r.kn = min(p.cps, p.n_k - r.k0);
+    r.v0 = r.vn = 0;
+  } else {
+    r.k0 = r.kn = 0;
+    r.v0 = p.cps * (s - p.n_ks);
+    r.vn = min(p.cps, p.n_vc - r.v0);
+  }
+  return r;
 }
 
 struct SegmentInfo {
@@ -201,6 +246,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
   uint8_t* sB = smem + p.off_b;
   uint8_t* sP = smem + p.off_p;
   float* red_max = reinterpret_cast<float*>(smem + p.off_red);   // [2][4][32]
+  ulonglong2* s_kinfo = reinterpret_cast<ulonglong2*>(smem + p.off_kinfo);   // [n_k]: the two rebuild words
   float* red_sum = red_max + 2 * 4 * 32;                          // [4][32]
   int* flags = reinterpret_cast<int*>(red_sum + 4 * 32);          // [2][4]
   float* head_s = reinterpret_cast<float*>(flags + 8);            // [32] per-head alpha or 1 / sum
@@ -257,6 +303,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     if (lane < kProducerLanes && has_work) {
       constexpr unsigned kLanes = (1u << kProducerLanes) - 1;
       int fills = 0;
+      int fill_st = 0, fill_rnd = 0;   // fills % S and fills / S, kept incrementally
       bool ok = true;
       // Where this lane's box of a tile comes from: chunked layout, tokens [box_rows lane, box_rows (lane + 1)) of the
       // tile (lanes < n_pieces); page layout, piece lane % n_pieces (of chunk lane / n_pieces). One block-table read
@@ -272,64 +319,78 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         if (pg < npages) bp.blk = __ldg(p.block_table + static_cast<long long>(c.si.b) * p.bt_stride + pg);
         return bp;
       };
-      // one stage: chunks [chunk0, chunk0 + nch) (column col0 on), lane 0 waits for the slot and arms its barrier,
-      // then every lane issues its box in the same instruction
-      auto load_stage = [&](const BoxPos& bp, int col0, int chunk0, int nch) -> bool {
-        const int st = fills % S;
-        const int rnd = fills / S;
-        bool got = true;
-        if (lane == 0 && rnd > 0)
-          got = mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
-        if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) return false;
-        if (lane == 0) mbar_arrive_expect_tx(&bars[bFull + st], nch * kTile * 128);
-        __syncwarp(kLanes);
-        uint8_t* dst = ring + st * p.stage_bytes;
-        if constexpr (kChunked) {
-          // 5-D box {64 columns, 8 rows, nch chunks, box_rows / 8 row groups, 1 block}: every 8-row group lands one atom
-          // (nch chunks of 1 KB) after the previous one, so a stage's atoms are nch KB apart
-          if (lane < p.n_pieces)
-            tma_load_5d(dst + lane * (p.box_rows / 8) * nch * p.chunk_stride, &maps.cache[nch - 1], &bars[bFull + st], 0,
-                        0, chunk0, bp.row / 8, bp.blk);
-        } else if (lane < nch * p.n_pieces) {
-          const int h = lane / p.n_pieces, pc = lane - h * p.n_pieces;
-          tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st],
-                      col0 + 64 * h, bp.row, bp.blk);
+      // One iteration of the plan: the key chunks of a tile (box positions pk; none when !has_k) and the value chunks
+      // of the tile before it (pv; none when !has_v). Per stage, lane 0 waits for the slot and arms its barrier with
+      // the bytes of both parts, then every lane issues its boxes in the same instruction. The key part lands first
+      // in the stage, the value part after the planned key part (kn chunks of the plan x 16 KB on).
+      auto load_iteration = [&](bool has_k, const BoxPos& pk, bool has_v, const BoxPos& pv) -> bool {
+        for (int s = 0; s < p.n_plan; ++s) {
+          const StagePart sp = plan_stage(p, s);
+          const int nk = has_k ? sp.kn : 0, nv = has_v ? sp.vn : 0;
+          if (nk + nv == 0) continue;
+          const int st = fill_st;
+          const int rnd = fill_rnd;
+          bool got = true;
+          if (lane == 0 && rnd > 0)
+            got = mbar_wait(&bars[bEmpty + st], (rnd - 1) & 1, abort_flag, p.err, kErrTimeoutProducer);
+          if (!__shfl_sync(kLanes, got ? 1 : 0, 0)) return false;
+          if (lane == 0) mbar_arrive_expect_tx(&bars[bFull + st], (nk + nv) * kTile * 128);
+          __syncwarp(kLanes);
+          uint8_t* dst = ring + st * p.stage_bytes;
+          uint8_t* dst_v = dst + sp.kn * kTile * 128;   // after the planned key part, present or not
+          if constexpr (kChunked) {
+            // 5-D box {64 columns, 8 rows, n chunks, box_rows / 8 row groups, 1 block}: every 8-row group lands one
+            // atom (n chunks of 1 KB) after the previous one, so a part's atoms are n KB apart
+            if (lane < p.n_pieces) {
+              if (nk)
+                tma_load_5d(dst + lane * (p.box_rows / 8) * nk * p.chunk_stride, &maps.cache[nk - 1],
+                            &bars[bFull + st], 0, 0, sp.k0, pk.row / 8, pk.blk);
+              if (nv)
+                tma_load_5d(dst_v + lane * (p.box_rows / 8) * nv * p.chunk_stride, &maps.cache[nv - 1],
+                            &bars[bFull + st], 0, 0, p.v_chunk0 + sp.v0, pv.row / 8, pv.blk);
+            }
+          } else {
+            // 3-D boxes of box_rows rows x 64 columns: box b is piece b % n_pieces of the stage's chunk b / n_pieces
+            // (n_pieces divides 16, so every box of a lane has the lane's piece)
+            for (int b = lane; b < (nk + nv) * p.n_pieces; b += kProducerLanes) {
+              const int h = b / p.n_pieces, pc = b - h * p.n_pieces;
+              const bool key = h < nk;
+              const BoxPos& bp = key ? pk : pv;
+              const int col = key ? 64 * (sp.k0 + h) : p.v_offset + 64 * (sp.v0 + h - nk);
+              tma_load_3d(dst + h * p.chunk_stride + pc * p.box_rows * 128, &maps.cache[0], &bars[bFull + st], col,
+                          bp.row, bp.blk);
+            }
+          }
+          ++fills;
+          if (++fill_st == S) {
+            fill_st = 0;
+            ++fill_rnd;
+          }
         }
-        ++fills;
         return true;
       };
       TileCursor kc, vc;
       kc.begin(p, seg_begin, seg_end);
       vc.begin(p, seg_begin, seg_end);
       BoxPos pos_k{}, pos_v{};
-      auto load_K = [&]() -> bool {
-        pos_k = box_pos(kc);
-        for (int k = 0; k < p.n_ks; ++k)
-          if (!load_stage(pos_k, 64 * p.cps * k, p.cps * k, min(p.cps, p.n_k - p.cps * k))) return false;
-        return true;
-      };
-      auto load_V = [&](const BoxPos& bp) -> bool {
-        for (int k = 0; k < p.n_vs; ++k)
-          if (!load_stage(bp, p.v_offset + 64 * p.cps * k, p.v_chunk0 + p.cps * k, min(p.cps, p.n_vc - p.cps * k)))
-            return false;
-        return true;
-      };
-      // stage order K(0), K(1), V(0), K(2), V(1), ...: V(i) reuses the box positions computed for K(i). (Taking V(i)
-      // before K(i + 1) where tile i + 1 opens a segment was measured 4 % slower: the MMA issuer then idles while the
-      // softmax finishes tile i, with the ring full of value stages.)
+      // iteration order: K(0); K(1) + V(0); K(2) + V(1); ...; V(last): V(i) reuses the box positions computed for
+      // K(i). (Taking V(i) before K(i + 1) where tile i + 1 opens a segment was measured 4 % slower: the MMA issuer
+      // then idles while the softmax finishes tile i, with the ring full of value stages.)
       if (kc.valid) {
-        ok = load_K();
+        pos_k = box_pos(kc);
+        ok = load_iteration(true, pos_k, false, pos_v);
         pos_v = pos_k;
         kc.next(p);
       }
       while (ok && vc.valid) {
         const BoxPos cur_v = pos_v;
-        if (kc.valid) {
-          if (!(ok = load_K())) break;
+        const bool has_k = kc.valid;
+        if (has_k) pos_k = box_pos(kc);
+        if (!(ok = load_iteration(has_k, pos_k, true, cur_v))) break;
+        if (has_k) {
           pos_v = pos_k;
           kc.next(p);
         }
-        if (!(ok = load_V(cur_v))) break;
         vc.next(p);
       }
       if (lane == 0 && *abort_flag) {
@@ -345,16 +406,25 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       constexpr uint32_t idK = idesc_bf16(128, 64, 0, 0);   // RoPE-key rebuild
       constexpr uint32_t idV = idesc_bf16(128, 32, 1, 1);   // O^T += V^T P, both MN-major
       const uint32_t ring_a = smem_u32(ring), q_a = smem_u32(sQ), b_a = smem_u32(sB), p_a = smem_u32(sP);
-      int fills = 0, qsegs = 0, vsegs = 0;
+      int qsegs = 0, vsegs = 0;
+      int slot = 0;             // the next stage to consume and the parity of its fill (no division by S)
+      uint32_t slot_par = 0;
       bool ok = true;
       auto wait = [&](int bar, uint32_t parity) -> bool {
         return mbar_wait(&bars[bar], parity, abort_flag, p.err, kErrTimeoutMma);
       };
       auto full = [&](int& st) -> bool {
-        st = fills % S;
-        if (!wait(bFull + st, (fills / S) & 1)) return false;
+        st = slot;
+        if (!wait(bFull + st, slot_par)) return false;
         tc_fence_after();
         return true;
+      };
+      auto release = [&](int st) {   // the stage's MMAs are all issued: its slot is free once they complete
+        mma_commit(&bars[bEmpty + st]);
+        if (++slot == S) {
+          slot = 0;
+          slot_par ^= 1u;
+        }
       };
       // Descriptors (16-byte units): every operand's high word is fixed, a K step only moves the low word.
       constexpr uint32_t hiQ = desc_hi(1024, kSwizzle128);          // query chunks: 8 rows = 1 KB
@@ -369,52 +439,100 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       // chunked layout: a stage of nch chunks holds 8-token atoms of nch KB (the producer's boxes stack them densely);
       // page layout: chunks of 128 rows, atoms of 1 KB whatever the stage holds
       auto atom_of = [&](int nch) -> int { return kChunked ? nch * p.chunk_stride : p.atom_stride; };
-      // key part of tile i: scores into S[i & 1] and the rebuilt RoPE keys
-      auto mma_K = [&](const TileCursor& c, int i) -> bool {
-        if (c.first()) {
-          if (!wait(bQFull, qsegs & 1)) return false;
-          ++qsegs;
+      // key chunks [c0, c1) of tile i in the stage at a0: per chunk its four score steps into S[i & 1], then the
+      // rebuild steps among them (a step holding RoPE coordinates: same A, the group's image as B), read from the
+      // chunk's info words, so no per-group loop bookkeeping sits between two MMA issues. (Measured against the
+      // previous per-group loop over each stage's steps: config-3 layers 2-5 % faster, c25 rows 10 %; each rebuild
+      // issued right after its score step: 1 % slower than after the chunk's scores.)
+      auto mma_key_chunks = [&](int i, uint32_t a0, int c0, int c1) {
+        const uint32_t dS = tmem + 32 * (i & 1);
+        const uint32_t hiSw = desc_hi(atom_of(c1 - c0), kSwizzle128);
+        for (int cc = c0; cc < c1; ++cc) {
+          const ulonglong2 rb = s_kinfo[cc];
+          const uint32_t ac = a0 + (cc - c0) * chunk16;
+          const uint32_t bq = loQ + cc * (kQChunkBytes >> 4);
+#pragma unroll
+          for (int s16 = 0; s16 < 4; ++s16)
+            mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
+#pragma unroll
+          for (int s16 = 0; s16 < 4; ++s16) {
+            const uint64_t da = desc_of(ac + s16 * 2, hiSw);
+            const uint32_t f = static_cast<uint32_t>(rb.x >> (16 * s16)) & 0xFFFFu;
+            if (f & 0x8000u)
+              mma_ss(tmem + kTmemK + 64 * (f & 3u), da, desc_of(loImg + ((f >> 2) & 63u) * (kKstBytes >> 4), hiImg), idK,
+                     (f >> 14) & 1u);
+            const uint32_t f2 = static_cast<uint32_t>(rb.y >> (16 * s16)) & 0xFFFFu;
+            if (f2 & 0x8000u)
+              mma_ss(tmem + kTmemK + 64 * (f2 & 3u), da, desc_of(loImg + ((f2 >> 2) & 63u) * (kKstBytes >> 4), hiImg),
+                     idK, (f2 >> 14) & 1u);
+          }
         }
-        const int sb = i & 1;
-        if (i >= 2 && !wait(bSFree + sb, ((i >> 1) - 1) & 1)) return false;
-        // The previous tile's RoPE-score MMAs read the rotated keys from the TMEM columns this tile's rebuild
-        // overwrites: they were issued before, and tcgen05.mma operations of one thread execute in issue order, so
-        // no wait (a wait here would drain the tensor pipe once per tile).
-        tc_fence_after();
-        const uint32_t dS = tmem + 32 * sb;
-        for (int k = 0; k < p.n_ks; ++k) {
+      };
+      // value chunks [v0, v0 + nv) of tile i in the stage part at av: O^T += V^T P for the O blocks whose chunk pair
+      // lies in this part, 128 latent columns (two chunks) at a time
+      auto mma_value_chunks = [&](const TileCursor& c, int i, uint32_t av, int v0, int nv) {
+        const uint32_t p0 = loP + (i & 1) * (kPBytes >> 4);
+        const uint32_t first = c.first() ? 1u : 0u;
+        const uint32_t hiSw = desc_hi(atom_of(nv), kSwizzle128);
+        const uint32_t pv_step16 = (2 * atom_of(nv)) >> 4;
+        const int j0 = (v0 + p.v_shift) >> 1, j1 = (v0 + nv + p.v_shift + 1) >> 1;
+        for (int j = j0; j < j1; ++j) {
+          // the pair's first chunk 2j - v_shift sits at position 2j - v_shift - v0 of the part (-1: the key chunk
+          // before the part, whose rows of O^T are never read)
+          const uint32_t aj = av + (2 * j - p.v_shift - v0) * chunk16;
+          const uint32_t dO = tmem + kTmemO + 32 * j;
+#pragma unroll
+          for (int s16 = 0; s16 < 8; ++s16)
+            // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
+            mma_ss(dO, desc_of(aj + s16 * pv_step16, hiSw), desc_of(p0 + s16 * (1024 >> 4), hiP), idV,
+                   (first && s16 == 0) ? 0u : 1u);
+        }
+      };
+      TileCursor kc, vc;
+      // One iteration of the plan: the key chunks of tile ik (cursor kc; none when !has_k), then the value chunks of
+      // tile iv (cursor vc; none when !has_v), stage by stage as the producer filled them.
+      auto mma_iteration = [&](bool has_k, int ik, bool has_v, int iv) -> bool {
+        if (has_k) {
+          if (kc.first()) {
+            if (!wait(bQFull, qsegs & 1)) return false;
+            ++qsegs;
+          }
+          const int sb = ik & 1;
+          if (ik >= 2 && !wait(bSFree + sb, ((ik >> 1) - 1) & 1)) return false;
+          // The previous tile's RoPE-score MMAs read the rotated keys from the TMEM columns this tile's rebuild
+          // overwrites: they were issued before, and tcgen05.mma operations of one thread execute in issue order, so
+          // no wait (a wait here would drain the tensor pipe once per tile).
+          tc_fence_after();
+        }
+        bool v_ready = false;
+        for (int s = 0; s < p.n_plan; ++s) {
+          const StagePart sp = plan_stage(p, s);
+          const int nk = has_k ? sp.kn : 0, nv = has_v ? sp.vn : 0;
+          if (nk + nv == 0) continue;
           int st;
           if (!full(st)) return false;
           const uint32_t a0 = loRing + st * stage16;
-          const int c0 = p.cps * k, c1 = min(p.n_k, c0 + p.cps);
-          const uint32_t hiSw = desc_hi(atom_of(c1 - c0), kSwizzle128);
-          for (int cc = c0; cc < c1; ++cc) {
-            const uint32_t ac = a0 + (cc - c0) * chunk16;
-            const uint32_t bq = loQ + cc * (kQChunkBytes >> 4);
-#pragma unroll
-            for (int s16 = 0; s16 < 4; ++s16)
-              mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
+          if (nk) {
+            mma_key_chunks(ik, a0, sp.k0, sp.k0 + nk);
+            if (sp.k0 + nk == p.n_k) mma_commit(&bars[bKrawFull]);
           }
-          // RoPE-key rebuild: every group's 16-column steps that fall in this stage's chunks (constant parameter offsets
-          // only, so nothing but arithmetic sits between two MMA issues)
-#pragma unroll
-          for (int g = 0; g < kG; ++g) {
-            const int ks0 = p.rope_ks0[g];
-            const int lo = max(ks0, 4 * c0), hi = min(p.rope_ks1[g], 4 * c1 - 1);
-            const uint32_t dK = tmem + kTmemK + 64 * g;
-            uint64_t da = desc_of(a0 + (lo / 4 - c0) * chunk16 + (lo % 4) * 2, hiSw);
-            uint64_t db = desc_of(loImg + (p.rope_e0[g] + lo - ks0) * (kKstBytes >> 4), hiImg);
-            for (int ks = lo; ks <= hi; ++ks) {
-              mma_ss(dK, da, db, idK, ks != ks0 ? 1u : 0u);
-              // next 16 columns: +32 bytes along the swizzled row, or the start of the next chunk
-              da += (ks % 4 == 3) ? chunk16 - 6 : 2;
-              db += kKstBytes >> 4;
+          if (nv) {
+            if (!v_ready) {
+              if (!wait(bPFull + (iv & 1), (iv >> 1) & 1)) return false;
+              if (vc.first()) {
+                if (vsegs > 0 && !wait(bOFree, (vsegs - 1) & 1)) return false;
+                ++vsegs;
+              }
+              tc_fence_after();
+              v_ready = true;
             }
+            // the value part sits after the planned key part even when this iteration has none, so that chunk -1 of
+            // a shifted pair always lies inside the stage
+            mma_value_chunks(vc, iv, loRingV + st * stage16 + sp.kn * (kTile * 128 >> 4), sp.v0, nv);
           }
-          mma_commit(&bars[bEmpty + st]);
-          ++fills;
+          release(st);
         }
-        mma_commit(&bars[bKrawFull]);
+        if (has_v) mma_commit(&bars[bPvDone + (iv & 1)]);
         return true;
       };
       // RoPE score of tile i once the rotation warps stored its keys
@@ -432,52 +550,16 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         if (c.last()) mma_commit(&bars[bQEmpty]);   // the segment's query chunks are read for the last time
         return true;
       };
-      // value part of tile i: O^T += V^T P, one 128-feature block (two chunks of a stage) at a time
-      auto mma_V = [&](const TileCursor& c, int i) -> bool {
-        const int pb = i & 1;
-        if (!wait(bPFull + pb, (i >> 1) & 1)) return false;
-        if (c.first()) {
-          if (vsegs > 0 && !wait(bOFree, (vsegs - 1) & 1)) return false;
-          ++vsegs;
-        }
-        tc_fence_after();
-        const uint32_t p0 = loP + pb * (kPBytes >> 4);
-        const uint32_t first = c.first() ? 1u : 0u;
-        for (int k = 0; k < p.n_vs; ++k) {
-          int st;
-          if (!full(st)) return false;
-          const uint32_t a0 = loRingV + st * stage16;
-          const int nchv = min(p.cps, p.n_vc - p.cps * k);
-          const uint32_t hiSw = desc_hi(atom_of(nchv), kSwizzle128);
-          const uint32_t pv_step16 = (2 * atom_of(nchv)) >> 4;
-          const int j0 = (p.cps * k) >> 1, j1 = min(p.n_vp, (p.cps * (k + 1)) >> 1);
-          for (int j = j0; j < j1; ++j) {
-            const uint32_t aj = a0 + (2 * j - p.cps * k) * chunk16;
-            const uint32_t dO = tmem + kTmemO + 32 * j;
-#pragma unroll
-            for (int s16 = 0; s16 < 8; ++s16)
-              // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
-              mma_ss(dO, desc_of(aj + s16 * pv_step16, hiSw), desc_of(p0 + s16 * (1024 >> 4), hiP), idV,
-                     (first && s16 == 0) ? 0u : 1u);
-          }
-          mma_commit(&bars[bEmpty + st]);
-          ++fills;
-        }
-        mma_commit(&bars[bPvDone + pb]);
-        return true;
-      };
-      TileCursor kc, vc;
       kc.begin(p, seg_begin, seg_end);
       vc.begin(p, seg_begin, seg_end);
       ok = wait(bImg, 0);   // the rotation warps' rebuild images
       if (ok && kc.valid) {
-        ok = mma_K(kc, 0) && mma_rope(kc, 0);
+        ok = mma_iteration(true, 0, false, 0) && mma_rope(kc, 0);
         kc.next(p);
       }
       for (int v = 0; ok && vc.valid; ++v) {
         const bool more = kc.valid;
-        if (more && !(ok = mma_K(kc, v + 1))) break;
-        if (!(ok = mma_V(vc, v))) break;
+        if (!(ok = mma_iteration(more, v + 1, true, v))) break;
         if (more) {
           if (!(ok = mma_rope(kc, v + 1))) break;
           kc.next(p);
@@ -542,6 +624,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             const int n = t >> 1, h = t & 1;
             *reinterpret_cast<uint4*>(sB + e * kKstBytes + (n >> 3) * 256 + h * 128 + (n & 7) * 16) = v[e];
           }
+        if (t < p.n_k) s_kinfo[t] = make_ulonglong2(p.k_rebuild[t][0], p.k_rebuild[t][1]);   // the issuer's rebuilds
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[bImg]);
@@ -770,8 +853,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             uint32_t o[32];
             tmem_ld32(tO + 32 * j, o);
             tmem_ld_wait();
-            const int f = 128 * j + row;
-            if (f < p.r_v) {
+            const int f = 128 * j - 64 * p.v_shift + row;   // block j starts at value chunk 2j - v_shift
+            if (f >= 0 && f < p.r_v) {
               float* dst = p.part + static_cast<long long>(s) * p.part_ss + f;
 #pragma unroll
               for (int h = 0; h < kH; ++h) dst[h * p.part_sh] = __uint_as_float(o[h]) * head_s[h];

@@ -35,6 +35,13 @@ struct DecodeParams {
   int box_rows, n_pieces;             // page layout: rows per box, boxes per chunk of a tile
   int n_k, n_ks;                      // key-part chunks and stages
   int v_offset, v_chunk0, r_v, n_vc, n_vs, n_vp;   // value part: first column (chunk), rank, chunks, stages, O blocks
+  // Stage plan of one iteration of the ring: the key chunks of tile i + 1, then the value chunks of tile i, in n_plan
+  // stages of at most `cps` chunks (plan_stage() in decode.cu). Packed: the n_k + n_vc chunks cut every cps chunks,
+  // so one stage can carry the end of the key part and the start of the value part; otherwise n_ks key stages, then
+  // n_vs value stages. O^T block j covers value chunks 2j - v_shift and 2j + 1 - v_shift (v_shift = 1 when the value
+  // part starts at an odd position of a packed plan, so that no block spans two stages; chunk -1 is a key chunk and
+  // feeds rows that are never read).
+  int packed, n_plan, v_shift;
   int n_kst;
   int kst_col[kDecodeMaxKsteps];
   int kst_src[kDecodeMaxKsteps];
@@ -44,10 +51,15 @@ struct DecodeParams {
   // per group: first and last 16-column step holding its RoPE coordinates, and the image of the first step (the
   // steps of a group are consecutive images)
   int rope_ks0[4], rope_ks1[4], rope_e0[4];
+  // per key chunk, the rebuild MMAs of its four 16-column steps (16 bits each, step s at bit 16 s): bit 15 a rebuild
+  // step, bit 14 accumulate (not the group's first step), bits 2-7 its image, bits 0-1 its group. Word 1 holds a
+  // second group's rebuild where one step holds the end of one group's RoPE coordinates and the start of the next
+  // (8-column aligned runs: at most two per step).
+  unsigned long long k_rebuild[kDecodeMaxQChunks - 4][2];
   float scale_log2;
   // shared-memory layout (byte offsets from the 1024-aligned base), set by the host launcher
   int stages;
-  int off_q, off_b, off_p, off_red, off_bars, smem_bytes;
+  int off_q, off_b, off_p, off_red, off_kinfo, off_bars, smem_bytes;
 };
 
 // Tensor maps of one decode launch: the cache (page layout: cache[0] only; chunked layout: cache[n - 1] fetches n
@@ -60,6 +72,8 @@ struct DecodeMaps {
 cudaError_t launch_latent_decode(const DecodeMaps& maps, const DecodeParams& p, int num_ctas, cudaStream_t stream);
 // Fills p.stages and the shared-memory offsets; returns false if the layout does not fit.
 bool decode_plan_smem(DecodeParams& p);
+// Chooses the stage plan (packed, n_plan, v_shift, n_vp) from n_k, n_vc, cps, n_ks and n_vs.
+void decode_plan_stages(DecodeParams& p);
 
 // Out[t, g * hpg + j, n] = X[t, g * hpg + j, :] @ W[g, :, n] for n in the group's column runs, 0 elsewhere.
 struct GroupGemmParams {

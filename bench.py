@@ -1033,6 +1033,16 @@ def main():
                          "traffic": traffic_per_launch, "traffic_source": traffic and traffic.get("source")},
             "clocks": clk,
             "gpu_launches": wl.launches_per_step * args.steps}
+    # the decode kernel's fraction per K rank (layers of one rank share a row layout and a stage plan)
+    by_rank = {}
+    for l in range(wl.L):
+        r = by_rank.setdefault(str(wl.weights[l].layout["lk"]), [0.0, 0.0, 0])
+        r[0] += kern_bytes[l]
+        r[1] += kern_ms[l]
+        r[2] += 1
+    line["roofline"]["frac_by_k_rank"] = {
+        k: {"layers": n, "us_per_launch": 1000.0 * t / n, "frac": b / (t / 1000.0) / 1e9 / peak_gbs}
+        for k, (b, t, n) in sorted(by_rank.items(), key=lambda kv: int(kv[0]))}
     if rank_gbs is not None:
         line["roofline"]["achieved_per_rank"] = rank_gbs[0]
     if not args.no_e2e:
