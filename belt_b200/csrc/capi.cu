@@ -623,7 +623,9 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   }
   if (!planned)
     return fail(BELT_ERR_INVALID, "latent_decode: layout (n_k %d, %d rebuild steps) does not fit in shared memory", n_k, nk);
-  decode_plan_stages(p);
+  if (!decode_plan_stages(p))
+    return fail(BELT_ERR_INVALID, "latent_decode: %d key and %d value chunks need more than %d ring stages", n_k, p.n_vc,
+                kDecodeMaxPlan);
   const bool use_chunked = p.chunked != 0;
 
   DecodeMaps maps;

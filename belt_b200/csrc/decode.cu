@@ -36,6 +36,8 @@
 //
 // Every wait is bounded (common.cuh): a logic error records a code in the device error word and the CTA drains what
 // it issued, frees its tensor memory and exits.
+#include <algorithm>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -76,8 +78,12 @@ constexpr int kNumBars = 32;
 static_assert(bImg < kNumBars, "barriers");
 // red_max [2][4][32], red_sum [4][32], flags [2][4], per-head alpha / 1 / sum [32]
 constexpr int kRedFloats = 2 * 4 * 32 + 4 * 32 + 2 * 4 + 32;
-constexpr int kKinfoBytes = 256;                // DecodeParams::k_rebuild, copied to shared memory at start
+// the issuer's tables, copied to shared memory at start: DecodeParams::k_rebuild, then DecodeParams::plan
+constexpr int kKinfoBytes = 192;
+constexpr int kPlanOff = kKinfoBytes;
+constexpr int kTablesBytes = 512;
 static_assert(kKinfoBytes >= (kDecodeMaxQChunks - 4) * 16, "k_rebuild");
+static_assert(kPlanOff + kDecodeMaxPlan * 16 <= kTablesBytes, "plan");
 }  // namespace dec
 
 bool decode_plan_smem(DecodeParams& p) {
@@ -85,7 +91,7 @@ bool decode_plan_smem(DecodeParams& p) {
   auto up = [](int x, int a) { return (x + a - 1) / a * a; };
   const int q_bytes = up((p.n_k + kG) * kQChunkBytes + 1024, 1024);
   const int b_bytes = p.n_kst * kKstBytes;
-  const int fixed = q_bytes + b_bytes + 2 * kPBytes + up(kRedFloats * 4, 128) + kKinfoBytes + kNumBars * 8 + 16 + 1024;
+  const int fixed = q_bytes + b_bytes + 2 * kPBytes + up(kRedFloats * 4, 128) + kTablesBytes + kNumBars * 8 + 16 + 1024;
   int stages = (kMaxSmem - fixed) / p.stage_bytes;
   if (stages > kMaxStages) stages = kMaxStages;
   if (stages < 2) return false;
@@ -95,12 +101,12 @@ bool decode_plan_smem(DecodeParams& p) {
   p.off_p = p.off_b + b_bytes;
   p.off_red = p.off_p + 2 * kPBytes;
   p.off_kinfo = p.off_red + up(kRedFloats * 4, 128);
-  p.off_bars = p.off_kinfo + kKinfoBytes;
+  p.off_bars = p.off_kinfo + kTablesBytes;
   p.smem_bytes = p.off_bars + kNumBars * 8 + 16 + 1024;
   return p.smem_bytes <= kMaxSmem;
 }
 
-void decode_plan_stages(DecodeParams& p) {
+bool decode_plan_stages(DecodeParams& p) {
   // Packed: the iteration's n_k key chunks and n_vc value chunks as one run cut every `cps` chunks. The value part
   // starts at position n_k; its O^T blocks are chunk pairs starting at even positions (v_shift = n_k % 2), so a pair
   // never spans two stages (cps is even). Separate (when a shifted value part would need more O^T blocks than TMEM
@@ -111,6 +117,34 @@ void decode_plan_stages(DecodeParams& p) {
   p.v_shift = p.packed ? shift : 0;
   p.n_vp = (p.n_vc + p.v_shift + 1) / 2;
   p.n_plan = p.packed ? (p.n_k + p.n_vc + p.cps - 1) / p.cps : p.n_ks + p.n_vs;
+  if (p.n_plan > kDecodeMaxPlan) return false;
+  // the issuer's words, from the same arithmetic as plan_stage()
+  auto atom_of = [&](int nch) { return p.chunked ? nch * p.chunk_stride : p.atom_stride; };
+  for (int s = 0; s < p.n_plan; ++s) {
+    int k0, kn, v0, vn;
+    if (p.packed) {
+      const int lo = s * p.cps, hi = std::min(lo + p.cps, p.n_k + p.n_vc);
+      k0 = lo;
+      kn = std::max(std::min(hi, p.n_k) - lo, 0);
+      v0 = std::max(lo - p.n_k, 0);
+      vn = std::max(hi - std::max(lo, p.n_k), 0);
+    } else if (s < p.n_ks) {
+      k0 = p.cps * s;
+      kn = std::min(p.cps, p.n_k - k0);
+      v0 = vn = 0;
+    } else {
+      k0 = kn = 0;
+      v0 = p.cps * (s - p.n_ks);
+      vn = std::min(p.cps, p.n_vc - v0);
+    }
+    const int j0 = (v0 + p.v_shift) >> 1, j1 = vn ? (v0 + vn + p.v_shift + 1) >> 1 : j0;
+    p.plan[s][0] = static_cast<unsigned>(k0 | kn << 8 | v0 << 16 | vn << 24);
+    p.plan[s][1] = kn ? desc_hi(static_cast<uint32_t>(atom_of(kn)), kSwizzle128) : 0u;
+    p.plan[s][2] = vn ? desc_hi(static_cast<uint32_t>(atom_of(vn)), kSwizzle128) : 0u;
+    p.plan[s][3] = static_cast<unsigned>(kn * (dec::kTile * 128 >> 4) | j0 << 16 | j1 << 20 |
+                                         (kn && k0 + kn == p.n_k ? 1 << 24 : 0));
+  }
+  return true;
 }
 
 // Stage s of an iteration's plan: key chunks [k0, k0 + kn), value chunks [v0, v0 + vn) (an absent part has n = 0).
@@ -247,6 +281,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
   uint8_t* sP = smem + p.off_p;
   float* red_max = reinterpret_cast<float*>(smem + p.off_red);   // [2][4][32]
   ulonglong2* s_kinfo = reinterpret_cast<ulonglong2*>(smem + p.off_kinfo);   // [n_k]: the two rebuild words
+  uint4* s_plan = reinterpret_cast<uint4*>(smem + p.off_kinfo + kPlanOff);     // [n_plan]: the issuer's stage words
   float* red_sum = red_max + 2 * 4 * 32;                          // [4][32]
   int* flags = reinterpret_cast<int*>(red_sum + 4 * 32);          // [2][4]
   float* head_s = reinterpret_cast<float*>(flags + 8);            // [32] per-head alpha or 1 / sum
@@ -444,13 +479,11 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       // chunk's info words, so no per-group loop bookkeeping sits between two MMA issues. (Measured against the
       // previous per-group loop over each stage's steps: config-3 layers 2-5 % faster, c25 rows 10 %; each rebuild
       // issued right after its score step: 1 % slower than after the chunk's scores.)
-      auto mma_key_chunks = [&](int i, uint32_t a0, int c0, int c1) {
+      auto mma_key_chunks = [&](int i, uint32_t a0, int c0, int c1, uint32_t hiSw) {
         const uint32_t dS = tmem + 32 * (i & 1);
-        const uint32_t hiSw = desc_hi(atom_of(c1 - c0), kSwizzle128);
-        for (int cc = c0; cc < c1; ++cc) {
+        uint32_t ac = a0, bq = loQ + c0 * (kQChunkBytes >> 4);
+        for (int cc = c0; cc < c1; ++cc, ac += chunk16, bq += kQChunkBytes >> 4) {
           const ulonglong2 rb = s_kinfo[cc];
-          const uint32_t ac = a0 + (cc - c0) * chunk16;
-          const uint32_t bq = loQ + cc * (kQChunkBytes >> 4);
 #pragma unroll
           for (int s16 = 0; s16 < 4; ++s16)
             mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
@@ -470,17 +503,14 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       };
       // value chunks [v0, v0 + nv) of tile i in the stage part at av: O^T += V^T P for the O blocks whose chunk pair
       // lies in this part, 128 latent columns (two chunks) at a time
-      auto mma_value_chunks = [&](const TileCursor& c, int i, uint32_t av, int v0, int nv) {
+      auto mma_value_chunks = [&](const TileCursor& c, int i, uint32_t av, int v0, uint32_t hiSw, int j0, int j1) {
         const uint32_t p0 = loP + (i & 1) * (kPBytes >> 4);
         const uint32_t first = c.first() ? 1u : 0u;
-        const uint32_t hiSw = desc_hi(atom_of(nv), kSwizzle128);
-        const uint32_t pv_step16 = (2 * atom_of(nv)) >> 4;
-        const int j0 = (v0 + p.v_shift) >> 1, j1 = (v0 + nv + p.v_shift + 1) >> 1;
-        for (int j = j0; j < j1; ++j) {
-          // the pair's first chunk 2j - v_shift sits at position 2j - v_shift - v0 of the part (-1: the key chunk
-          // before the part, whose rows of O^T are never read)
-          const uint32_t aj = av + (2 * j - p.v_shift - v0) * chunk16;
-          const uint32_t dO = tmem + kTmemO + 32 * j;
+        const uint32_t pv_step16 = 2 * (hiSw & 0x3FFFu);   // 16 tokens = two atoms (the SBO field, in 16-byte units)
+        // the pair's first chunk 2j - v_shift sits at position 2j - v_shift - v0 of the part (-1: the key chunk before
+        // the part, whose rows of O^T are never read)
+        uint32_t aj = av + (2 * j0 - p.v_shift - v0) * chunk16, dO = tmem + kTmemO + 32 * j0;
+        for (int j = j0; j < j1; ++j, aj += 2 * chunk16, dO += 32) {
 #pragma unroll
           for (int s16 = 0; s16 < 8; ++s16)
             // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
@@ -506,15 +536,16 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         }
         bool v_ready = false;
         for (int s = 0; s < p.n_plan; ++s) {
-          const StagePart sp = plan_stage(p, s);
-          const int nk = has_k ? sp.kn : 0, nv = has_v ? sp.vn : 0;
+          const uint4 pl = s_plan[s];   // the stage's word (decode_plan_stages)
+          const int nk = has_k ? (pl.x >> 8) & 0xFF : 0, nv = has_v ? pl.x >> 24 : 0;
           if (nk + nv == 0) continue;
           int st;
           if (!full(st)) return false;
           const uint32_t a0 = loRing + st * stage16;
           if (nk) {
-            mma_key_chunks(ik, a0, sp.k0, sp.k0 + nk);
-            if (sp.k0 + nk == p.n_k) mma_commit(&bars[bKrawFull]);
+            const int k0 = pl.x & 0xFF;
+            mma_key_chunks(ik, a0, k0, k0 + nk, pl.y);
+            if (pl.w & (1u << 24)) mma_commit(&bars[bKrawFull]);
           }
           if (nv) {
             if (!v_ready) {
@@ -528,7 +559,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             }
             // the value part sits after the planned key part even when this iteration has none, so that chunk -1 of
             // a shifted pair always lies inside the stage
-            mma_value_chunks(vc, iv, loRingV + st * stage16 + sp.kn * (kTile * 128 >> 4), sp.v0, nv);
+            mma_value_chunks(vc, iv, loRingV + st * stage16 + (pl.w & 0xFFFFu), (pl.x >> 16) & 0xFF, pl.z,
+                             (pl.w >> 16) & 0xF, (pl.w >> 20) & 0xF);
           }
           release(st);
         }
@@ -625,6 +657,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
             *reinterpret_cast<uint4*>(sB + e * kKstBytes + (n >> 3) * 256 + h * 128 + (n & 7) * 16) = v[e];
           }
         if (t < p.n_k) s_kinfo[t] = make_ulonglong2(p.k_rebuild[t][0], p.k_rebuild[t][1]);   // the issuer's rebuilds
+        if (t < p.n_plan) s_plan[t] = make_uint4(p.plan[t][0], p.plan[t][1], p.plan[t][2], p.plan[t][3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[bImg]);

@@ -11,6 +11,7 @@ namespace belt {
 constexpr int kDecodeMaxKsteps = 20;   // rebuild K-steps: <= 5 per group (64 coordinates at any 16-column offset)
 constexpr int kDecodeMaxVPairs = 5;    // O^T blocks of 128 latent columns: r_v <= 640
 constexpr int kDecodeMaxQChunks = 16;  // n_k + 4 query chunks of 64 columns: v_offset <= 768
+constexpr int kDecodeMaxPlan = 12;     // stages of one ring iteration: ceil((12 + 10) / 2) at 2 chunks a stage
 
 struct DecodeParams {
   const int32_t* block_table;
@@ -42,6 +43,10 @@ struct DecodeParams {
   // part starts at an odd position of a packed plan, so that no block spans two stages; chunk -1 is a key chunk and
   // feeds rows that are never read).
   int packed, n_plan, v_shift;
+  // the plan's stages for the MMA issuer, one 16-byte word each (decode_plan_stages): x = k0 | kn << 8 | v0 << 16 |
+  // vn << 24; y, z = the high descriptor words of the key and value parts' SWIZZLE_128B atoms; w = the value part's
+  // offset in the stage (16-byte units) | first O^T block << 16 | end block << 20 | 1 << 24 if the key part ends here
+  unsigned int plan[kDecodeMaxPlan][4];
   int n_kst;
   int kst_col[kDecodeMaxKsteps];
   int kst_src[kDecodeMaxKsteps];
@@ -72,8 +77,9 @@ struct DecodeMaps {
 cudaError_t launch_latent_decode(const DecodeMaps& maps, const DecodeParams& p, int num_ctas, cudaStream_t stream);
 // Fills p.stages and the shared-memory offsets; returns false if the layout does not fit.
 bool decode_plan_smem(DecodeParams& p);
-// Chooses the stage plan (packed, n_plan, v_shift, n_vp) from n_k, n_vc, cps, n_ks and n_vs.
-void decode_plan_stages(DecodeParams& p);
+// Chooses the stage plan (packed, n_plan, v_shift, n_vp, plan) from n_k, n_vc, cps, n_ks, n_vs and the layout;
+// false if it has more stages than kDecodeMaxPlan.
+bool decode_plan_stages(DecodeParams& p);
 
 // Out[t, g * hpg + j, n] = X[t, g * hpg + j, :] @ W[g, :, n] for n in the group's column runs, 0 elsewhere.
 struct GroupGemmParams {
