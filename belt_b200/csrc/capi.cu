@@ -580,6 +580,40 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
     }
     p.k_rebuild[cc][0] = v[0];
     p.k_rebuild[cc][1] = v[1];
+    // as runs: the chunk's rebuild steps as at most two runs of consecutive steps of one group with consecutive
+    // images; word 1 = bit 63 | run 0 | run 1 << 16, a run = bit 15 | step 0's accumulate flag << 14 | first image << 6
+    // | group << 4 | (count - 1) << 2 | first step. The issuer then emits each run without per-step tests.
+    struct Run { int step, count, group, image, acc; };
+    Run runs[8];
+    int n_runs = 0;
+    bool fits = true;
+    for (int s16 = 0; s16 < 4; ++s16)
+      for (int w = 0; w < 2; ++w) {
+        const unsigned f = static_cast<unsigned>(v[w] >> (16 * s16)) & 0xFFFFu;
+        if (!(f & 0x8000u)) continue;
+        const int g = static_cast<int>(f & 3u), e = static_cast<int>((f >> 2) & 63u), acc = (f >> 14) & 1u;
+        bool joined = false;
+        for (int r = 0; r < n_runs && !joined; ++r)
+          if (runs[r].group == g && runs[r].step + runs[r].count == s16 && runs[r].image + runs[r].count == e && acc) {
+            ++runs[r].count;
+            joined = true;
+          }
+        if (!joined) {
+          if (n_runs == 8) fits = false;
+          else runs[n_runs++] = Run{s16, 1, g, e, static_cast<int>(acc)};
+        }
+      }
+    if (fits && n_runs > 0 && n_runs <= 2) {
+      unsigned long long word = 1ull << 63;
+      for (int r = 0; r < n_runs; ++r)
+        word |= static_cast<unsigned long long>(0x8000u | (static_cast<unsigned>(runs[r].acc) << 14) |
+                                                (static_cast<unsigned>(runs[r].image) << 6) |
+                                                (static_cast<unsigned>(runs[r].group) << 4) |
+                                                (static_cast<unsigned>(runs[r].count - 1) << 2) |
+                                                static_cast<unsigned>(runs[r].step))
+                << (16 * r);
+      p.k_rebuild[cc][1] = word;
+    }
   }
   for (int e = 0; e < nk; ++e) {
     p.kst_col[e] = ks_list[e].col;

@@ -479,6 +479,34 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       // chunk's info words, so no per-group loop bookkeeping sits between two MMA issues. (Measured against the
       // previous per-group loop over each stage's steps: config-3 layers 2-5 % faster, c25 rows 10 %; each rebuild
       // issued right after its score step: 1 % slower than after the chunk's scores.)
+      // one run of rebuild steps of a chunk at ac (a run word of DecodeParams::k_rebuild; bit 15 clear: none): its MMAs
+      // unrolled by length, so no per-step test sits between two issues
+      auto mma_rebuild_run = [&](uint32_t w, uint32_t ac, uint32_t hiSw) {
+        if (!(w & 0x8000u)) return;
+        const uint32_t dK = tmem + kTmemK + 64 * ((w >> 4) & 3u);
+        const uint32_t a = ac + 2 * (w & 3u), b = loImg + ((w >> 6) & 63u) * (kKstBytes >> 4);
+        const uint32_t acc0 = (w >> 14) & 1u;
+        constexpr uint32_t kB = kKstBytes >> 4;
+        switch ((w >> 2) & 3u) {
+          case 3:
+            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
+            mma_ss(dK, desc_of(a + 4, hiSw), desc_of(b + 2 * kB, hiImg), idK, 1u);
+            mma_ss(dK, desc_of(a + 6, hiSw), desc_of(b + 3 * kB, hiImg), idK, 1u);
+            break;
+          case 2:
+            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
+            mma_ss(dK, desc_of(a + 4, hiSw), desc_of(b + 2 * kB, hiImg), idK, 1u);
+            break;
+          case 1:
+            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
+            break;
+          default:
+            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+        }
+      };
       auto mma_key_chunks = [&](int i, uint32_t a0, int c0, int c1, uint32_t hiSw) {
         const uint32_t dS = tmem + 32 * (i & 1);
         uint32_t ac = a0, bq = loQ + c0 * (kQChunkBytes >> 4);
@@ -487,6 +515,21 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
 #pragma unroll
           for (int s16 = 0; s16 < 4; ++s16)
             mma_ss(dS, desc_of(ac + s16 * 2, hiSw), desc_of(bq + s16 * 2, hiQ), idS, (cc | s16) ? 1u : 0u);
+          if (rb.y >> 63) {   // the chunk's rebuild steps as at most two runs (host-encoded)
+            const uint32_t w0 = static_cast<uint32_t>(rb.y) & 0xFFFFu;
+            if ((w0 & 0xCu) == 0xCu) {   // one run of all four steps (the common case): straight-line issue
+              const uint32_t dK = tmem + kTmemK + 64 * ((w0 >> 4) & 3u);
+              const uint32_t b = loImg + ((w0 >> 6) & 63u) * (kKstBytes >> 4);
+#pragma unroll
+              for (int s16 = 0; s16 < 4; ++s16)
+                mma_ss(dK, desc_of(ac + s16 * 2, hiSw), desc_of(b + s16 * (kKstBytes >> 4), hiImg), idK,
+                       s16 ? 1u : (w0 >> 14) & 1u);
+            } else {
+              mma_rebuild_run(w0, ac, hiSw);
+              mma_rebuild_run(static_cast<uint32_t>(rb.y >> 16) & 0xFFFFu, ac, hiSw);
+            }
+            continue;
+          }
 #pragma unroll
           for (int s16 = 0; s16 < 4; ++s16) {
             const uint64_t da = desc_of(ac + s16 * 2, hiSw);

@@ -59,7 +59,9 @@ struct DecodeParams {
   // per key chunk, the rebuild MMAs of its four 16-column steps (16 bits each, step s at bit 16 s): bit 15 a rebuild
   // step, bit 14 accumulate (not the group's first step), bits 2-7 its image, bits 0-1 its group. Word 1 holds a
   // second group's rebuild where one step holds the end of one group's RoPE coordinates and the start of the next
-  // (8-column aligned runs: at most two per step).
+  // (8-column aligned runs: at most two per step), or, with bit 63 set, the chunk's rebuild steps as at most two runs
+  // of consecutive steps (run r in bits 16 r .. 16 r + 15: bit 15 | step 0's accumulate flag << 14 | first image << 6
+  // | group << 4 | (count - 1) << 2 | first step), which the issuer emits without per-step tests.
   unsigned long long k_rebuild[kDecodeMaxQChunks - 4][2];
   float scale_log2;
   // shared-memory layout (byte offsets from the 1024-aligned base), set by the host launcher
