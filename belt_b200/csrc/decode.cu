@@ -553,13 +553,19 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
         // the pair's first chunk 2j - v_shift sits at position 2j - v_shift - v0 of the part (-1: the key chunk before
         // the part, whose rows of O^T are never read)
         uint32_t aj = av + (2 * j0 - p.v_shift - v0) * chunk16, dO = tmem + kTmemO + 32 * j0;
-        for (int j = j0; j < j1; ++j, aj += 2 * chunk16, dO += 32) {
+        // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
+        auto block = [&](uint32_t a, uint32_t d) {
 #pragma unroll
           for (int s16 = 0; s16 < 8; ++s16)
-            // A = V^T (MN-major SW128, 16 tokens = 2 atoms per step), B = P (MN-major, 16 tokens = 1 KB per step)
-            mma_ss(dO, desc_of(aj + s16 * pv_step16, hiSw), desc_of(p0 + s16 * (1024 >> 4), hiP), idV,
+            mma_ss(d, desc_of(a + s16 * pv_step16, hiSw), desc_of(p0 + s16 * (1024 >> 4), hiP), idV,
                    (first && s16 == 0) ? 0u : 1u);
+        };
+        if (j1 - j0 == 2) {   // a full stage: both blocks straight-line
+          block(aj, dO);
+          block(aj + 2 * chunk16, dO + 32);
+          return;
         }
+        for (int j = j0; j < j1; ++j, aj += 2 * chunk16, dO += 32) block(aj, dO);
       };
       TileCursor kc, vc;
       // One iteration of the plan: the key chunks of tile ik (cursor kc; none when !has_k), then the value chunks of
