@@ -15,7 +15,11 @@
 //   i+1's key chunks are scored and tile i's values stream in. One iteration's key and value chunks are packed into
 //   full stages (a stage may end one part and start the next: the host's stage plan, decode_plan_stages), so a row
 //   of 16 chunks takes 4 stages of 64 KB whatever its K / V split.
-// * warp 1, tcgen05 issuer (one thread; descriptors advance only their low words), M = 128 tokens:
+// * warp 1, tcgen05 issuer (one thread; descriptors advance only their low words), M = 128 tokens. The pipe does not
+//   queue MMAs, so this thread's instruction stream bounds the tile: it walks host-computed tables (per-stage plan words,
+//   per-chunk rebuild runs; DecodeParams::plan / k_rebuild, copied to shared memory at the start) instead of computing
+//   chunk ranges, descriptor words and rebuild steps between issues.
+//
 //     - scores S[tok, head] (N = 32: 24 heads; the last 8 columns are ignored) over the K part against the
 //       block-diagonal query;
 //     - the rebuilt RoPE keys gain * B_g c~_g: per group the 16-column K-steps holding its rr_g coordinates against
@@ -480,31 +484,21 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       // previous per-group loop over each stage's steps: config-3 layers 2-5 % faster, c25 rows 10 %; each rebuild
       // issued right after its score step: 1 % slower than after the chunk's scores.)
       // one run of rebuild steps of a chunk at ac (a run word of DecodeParams::k_rebuild; bit 15 clear: none): its MMAs
-      // unrolled by length, so no per-step test sits between two issues
+      // unrolled, one forward branch per further step
       auto mma_rebuild_run = [&](uint32_t w, uint32_t ac, uint32_t hiSw) {
         if (!(w & 0x8000u)) return;
         const uint32_t dK = tmem + kTmemK + 64 * ((w >> 4) & 3u);
         const uint32_t a = ac + 2 * (w & 3u), b = loImg + ((w >> 6) & 63u) * (kKstBytes >> 4);
         const uint32_t acc0 = (w >> 14) & 1u;
         constexpr uint32_t kB = kKstBytes >> 4;
-        switch ((w >> 2) & 3u) {
-          case 3:
-            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
-            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
+        const uint32_t n = (w >> 2) & 3u;   // the run's length - 1
+        mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+        if (n >= 1) {
+          mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
+          if (n >= 2) {
             mma_ss(dK, desc_of(a + 4, hiSw), desc_of(b + 2 * kB, hiImg), idK, 1u);
-            mma_ss(dK, desc_of(a + 6, hiSw), desc_of(b + 3 * kB, hiImg), idK, 1u);
-            break;
-          case 2:
-            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
-            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
-            mma_ss(dK, desc_of(a + 4, hiSw), desc_of(b + 2 * kB, hiImg), idK, 1u);
-            break;
-          case 1:
-            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
-            mma_ss(dK, desc_of(a + 2, hiSw), desc_of(b + kB, hiImg), idK, 1u);
-            break;
-          default:
-            mma_ss(dK, desc_of(a, hiSw), desc_of(b, hiImg), idK, acc0);
+            if (n == 3) mma_ss(dK, desc_of(a + 6, hiSw), desc_of(b + 3 * kB, hiImg), idK, 1u);
+          }
         }
       };
       auto mma_key_chunks = [&](int i, uint32_t a0, int c0, int c1, uint32_t hiSw) {
