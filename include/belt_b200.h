@@ -196,7 +196,7 @@ int belt_merge_up_project(const float* part, int64_t part_ss, int64_t part_sh, c
 
 /*
  * One decode step of a compressed layer with no caller-provided scratch: belt_decode_schedule_weighted (start cost
- * 10, the backend's split), belt_latent_decode and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
+ * 13, the backend's start cost; no speed balancing, which needs state across steps), belt_latent_decode and belt_merge_segments in a row on `stream`, with the segment records and split-KV partials kept in a fixed
  * 24 MiB array inside this library instead of buffers from the caller. It has no counterpart in the reference
  * (whose decode allocates its partials per call); it exists for callers that cannot allocate device memory: hosts
  * binding this ABI that hold only the engine's KV pool, query and output buffers, and engines that reserved nearly
