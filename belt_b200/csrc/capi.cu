@@ -603,7 +603,7 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
           else runs[n_runs++] = Run{s16, 1, g, e, static_cast<int>(acc)};
         }
       }
-    if (fits && n_runs > 0 && n_runs <= 2) {
+    if (fits && n_runs <= 2) {   // no run at all (a chunk without RoPE coordinates): bit 63 alone
       unsigned long long word = 1ull << 63;
       for (int r = 0; r < n_runs; ++r)
         word |= static_cast<unsigned long long>(0x8000u | (static_cast<unsigned>(runs[r].acc) << 14) |
