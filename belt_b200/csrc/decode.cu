@@ -68,8 +68,8 @@ constexpr int bFull = 0;                       // [kMaxStages]
 constexpr int bEmpty = bFull + kMaxStages;     // [kMaxStages]
 constexpr int bQFull = bEmpty + kMaxStages;
 constexpr int bQEmpty = bQFull + 1;
-constexpr int bKrawFull = bQEmpty + 1;
-constexpr int bKpeFull = bKrawFull + 1;
+constexpr int bKraw = bQEmpty + 1;            // [2]: the rebuilt keys of a wave of groups are in TMEM
+constexpr int bKpeFull = bKraw + 2;
 constexpr int bSFull = bKpeFull + 1;           // [2]
 constexpr int bSFree = bSFull + 2;             // [2]
 constexpr int bPFull = bSFree + 2;             // [2]
@@ -122,6 +122,22 @@ bool decode_plan_stages(DecodeParams& p) {
   p.n_vp = (p.n_vc + p.v_shift + 1) / 2;
   p.n_plan = p.packed ? (p.n_k + p.n_vc + p.cps - 1) / p.cps : p.n_ks + p.n_vs;
   if (p.n_plan > kDecodeMaxPlan) return false;
+  // Rotation waves. Where the key part spans three or more stages, the groups whose rebuild steps all lie before its
+  // last stage form wave 0 and the rotation of their keys starts a stage early (wave 1: the rest, after the key part);
+  // the rotation was measured on the critical path there (layers of r_k 576 and 640: 3-5 % faster). Elsewhere all
+  // groups form wave 0: one barrier per tile, committed after the key part (starting the rotation earlier there adds
+  // TMEM traffic during the key MMAs and measured 1-3 % slower).
+  p.kraw_wave = 0;
+  const int k_stages = p.packed ? (p.n_k + p.cps - 1) / p.cps : p.n_ks;
+  if (k_stages >= 3) {
+    const int last_chunk0 = (k_stages - 1) * p.cps;   // first key chunk of the key part's last stage
+    bool late = false;
+    for (int g = 0; g < kG; ++g) {
+      late = late || p.rope_ks1[g] / 4 >= last_chunk0;   // groups in order: once late, the rest are late too
+      if (late) p.kraw_wave |= 1 << g;
+    }
+    if (p.kraw_wave == 0xF) p.kraw_wave = 0;   // no early group: one wave
+  }
   // the issuer's words, from the same arithmetic as plan_stage()
   auto atom_of = [&](int nch) { return p.chunked ? nch * p.chunk_stride : p.atom_stride; };
   for (int s = 0; s < p.n_plan; ++s) {
@@ -145,8 +161,17 @@ bool decode_plan_stages(DecodeParams& p) {
     p.plan[s][0] = static_cast<unsigned>(k0 | kn << 8 | v0 << 16 | vn << 24);
     p.plan[s][1] = kn ? desc_hi(static_cast<uint32_t>(atom_of(kn)), kSwizzle128) : 0u;
     p.plan[s][2] = vn ? desc_hi(static_cast<uint32_t>(atom_of(vn)), kSwizzle128) : 0u;
-    p.plan[s][3] = static_cast<unsigned>(kn * (dec::kTile * 128 >> 4) | j0 << 16 | j1 << 20 |
-                                         (kn && k0 + kn == p.n_k ? 1 << 24 : 0));
+    // wave barriers: wave 0 is committed after the stage holding the last rebuild step of its last group, wave 1 after
+    // the key part's last stage
+    unsigned waves = 0;
+    if (kn) {
+      int last0 = -1;
+      for (int g = 0; g < kG; ++g)
+        if (!((p.kraw_wave >> g) & 1)) last0 = std::max(last0, p.rope_ks1[g] / 4);
+      if (last0 >= k0 && last0 < k0 + kn) waves |= 1u;
+      if (p.kraw_wave && k0 + kn == p.n_k) waves |= 2u;
+    }
+    p.plan[s][3] = static_cast<unsigned>(kn * (dec::kTile * 128 >> 4) | j0 << 16 | j1 << 20) | waves << 24;
   }
   return true;
 }
@@ -308,7 +333,8 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
     }
     mbar_init(&bars[bQFull], 1);
     mbar_init(&bars[bQEmpty], 1);
-    mbar_init(&bars[bKrawFull], 1);
+    mbar_init(&bars[bKraw], 1);
+    mbar_init(&bars[bKraw + 1], 1);
     mbar_init(&bars[bKpeFull], 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[bSFull + i], 1);
@@ -588,7 +614,9 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
           if (nk) {
             const int k0 = pl.x & 0xFF;
             mma_key_chunks(ik, a0, k0, k0 + nk, pl.y);
-            if (pl.w & (1u << 24)) mma_commit(&bars[bKrawFull]);
+            // the wave of groups whose last rebuild step is in this stage: its rotation can start once it completes
+            if (pl.w & (1u << 24)) mma_commit(&bars[bKraw]);
+            if (pl.w & (1u << 25)) mma_commit(&bars[bKraw + 1]);
           }
           if (nv) {
             if (!v_ready) {
@@ -721,11 +749,19 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 8; ++k) cs[k] = make_uint4(0, 0, 0, 0);
         }
-        const bool got = mbar_wait(&bars[bKrawFull], i & 1, abort_flag, p.err, kErrTimeoutEpilogue);
-        if (!__all_sync(0xffffffffu, got)) break;
-        tc_fence_after();
+        bool got = true;
+        int wave = -1;
 #pragma unroll 1
         for (int g = 0; g < kG; ++g) {
+          // each wave of groups as soon as its rebuild MMAs completed (wave 1 only where the key part spans three or
+          // more stages; elsewhere every group is in wave 0, one wait per tile)
+          const int wg = (p.kraw_wave >> g) & 1;
+          if (wg != wave) {
+            wave = wg;
+            got = __all_sync(0xffffffffu, mbar_wait(&bars[bKraw + wg], i & 1, abort_flag, p.err, kErrTimeoutEpilogue));
+            if (!got) break;
+            tc_fence_after();
+          }
           // all 64 fp32 channels are read before the packed BF16 keys overwrite the group's first 32 columns
           uint32_t x[32], y[32], o[32];
           tmem_ld32(tK + 64 * g, x);
@@ -769,6 +805,7 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
           }
           tmem_st32(tK + 64 * g, o);
         }
+        if (!got) break;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();

@@ -45,8 +45,10 @@ struct DecodeParams {
   int packed, n_plan, v_shift;
   // the plan's stages for the MMA issuer, one 16-byte word each (decode_plan_stages): x = k0 | kn << 8 | v0 << 16 |
   // vn << 24; y, z = the high descriptor words of the key and value parts' SWIZZLE_128B atoms; w = the value part's
-  // offset in the stage (16-byte units) | first O^T block << 16 | end block << 20 | 1 << 24 if the key part ends here
+  // offset in the stage (16-byte units) | first O^T block << 16 | end block << 20 | commit the rotation-wave barriers
+  // after this stage's key chunks << 24 (bit 0: wave 0, bit 1: wave 1)
   unsigned int plan[kDecodeMaxPlan][4];
+  int kraw_wave;                      // bit g: group g's keys are rotated in wave 1 (decode_plan_stages)
   int n_kst;
   int kst_col[kDecodeMaxKsteps];
   int kst_src[kDecodeMaxKsteps];
