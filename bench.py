@@ -861,10 +861,10 @@ class ServingRun:
                         c += 1
 
     def launches(self) -> int:
-        """This repository's kernel launches in ``run`` (the prefill chunks' projection GEMM is a library call and is
-        counted apart, in ``library_gemm_launches``)."""
+        """This repository's kernel launches in ``run``: per decode step the schedule and four per layer, per prefill
+        chunk and layer the projection GEMM (``belt_gemm_bf16``) and the cache write."""
         dec_steps = len(self.waves) * self.steps
-        return dec_steps * (1 + 4 * self.L) + sum(m["chunks"] for m in self.meta) * self.L
+        return dec_steps * (1 + 4 * self.L) + 2 * sum(m["chunks"] for m in self.meta) * self.L
 
 
 def run_serving(args, group, dev):
@@ -927,8 +927,7 @@ def run_serving(args, group, dev):
                        "hbm_gb_per_s_rank0": (dec_bytes + pf_bytes) / (ms_local / 1000.0) / 1e9,
                        "hbm_frac_rank0": (dec_bytes + pf_bytes) / (ms_local / 1000.0) / 1e9 / peak_gbs,
                        "l2": "inputs larger than L2 (wave buffers of tens of GB)"},
-            "roofline": None, "clocks": clk, "gpu_launches": run.launches(),
-            "library_gemm_launches": sum(m["chunks"] for m in run.meta) * run.L}
+            "roofline": None, "clocks": clk, "gpu_launches": run.launches()}
     if parity is not None:
         line["parity"] = parity
     if rank == 0:
