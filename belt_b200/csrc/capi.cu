@@ -526,7 +526,7 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   // rebuild K-steps: 16-column steps covering every group's [off, off + rr), read from its rope blocks; sorted by
   // column so that the steps of every key pair stage (128 columns) form one range
-  struct Kstep { int col, src, group, first; };
+  struct Kstep { int col, src, group; };
   Kstep ks_list[kDecodeMaxKsteps];
   int nb_first = 0, nk = 0;
   for (int g = 0; g < kG; ++g) {
@@ -537,7 +537,7 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
     for (int ks = off / 16; ks <= (off + rr - 1) / 16; ++ks) {
       if (nk >= kDecodeMaxKsteps) return fail(BELT_ERR_INVALID, "latent_decode: too many rebuild K-steps");
       const int col = 16 * ks;
-      ks_list[nk++] = Kstep{col, (nb_first + (col / 64 - c_lo)) * 64 + col % 64, g, ks == off / 16};
+      ks_list[nk++] = Kstep{col, (nb_first + (col / 64 - c_lo)) * 64 + col % 64, g};
     }
     nb_first += c_hi - c_lo + 1;
   }
@@ -615,23 +615,7 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
       p.k_rebuild[cc][1] = word;
     }
   }
-  for (int e = 0; e < nk; ++e) {
-    p.kst_col[e] = ks_list[e].col;
-    p.kst_src[e] = ks_list[e].src;
-    p.kst_group[e] = ks_list[e].group;
-    p.kst_first[e] = ks_list[e].first;
-  }
-  for (int k = 0; k < 8; ++k) {
-    p.ks_kst_begin[k] = p.ks_kst_end[k] = 0;
-    if (k >= p.n_ks) continue;
-    const int lo = 64 * p.cps * k, hi = 64 * p.cps * (k + 1);
-    int b = 0;
-    while (b < nk && ks_list[b].col < lo) ++b;
-    int e = b;
-    while (e < nk && ks_list[e].col < hi) ++e;
-    p.ks_kst_begin[k] = b;
-    p.ks_kst_end[k] = e;
-  }
+  for (int e = 0; e < nk; ++e) p.kst_src[e] = ks_list[e].src;   // the rotation warps build image e from these columns
   p.n_kst = nk;
   bool planned = decode_plan_smem(p);
   if (!planned && chunked) {   // two 64 KB stages do not fit next to this query / rebuild layout: 32 KB page stages
@@ -643,16 +627,6 @@ int latent_decode_impl(const void* q_bd, int32_t num_reqs, int32_t kq, const voi
     p.stage_bytes = p.cps * 128 * 128;
     p.n_ks = (n_k + p.cps - 1) / p.cps;
     p.n_vs = (p.n_vc + p.cps - 1) / p.cps;
-    for (int k = 0; k < 8; ++k) {
-      p.ks_kst_begin[k] = p.ks_kst_end[k] = 0;
-      if (k >= p.n_ks) continue;
-      int b = 0;
-      while (b < nk && ks_list[b].col < 128 * k) ++b;
-      int e = b;
-      while (e < nk && ks_list[e].col < 128 * (k + 1)) ++e;
-      p.ks_kst_begin[k] = b;
-      p.ks_kst_end[k] = e;
-    }
     planned = decode_plan_smem(p);
   }
   if (!planned)

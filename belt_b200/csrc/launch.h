@@ -50,11 +50,7 @@ struct DecodeParams {
   unsigned int plan[kDecodeMaxPlan][4];
   int kraw_wave;                      // bit g: group g's keys are rotated in wave 1 (decode_plan_stages)
   int n_kst;
-  int kst_col[kDecodeMaxKsteps];
-  int kst_src[kDecodeMaxKsteps];
-  int kst_group[kDecodeMaxKsteps];
-  int kst_first[kDecodeMaxKsteps];
-  int ks_kst_begin[8], ks_kst_end[8];  // rebuild K-steps (sorted by column) inside each key stage
+  int kst_src[kDecodeMaxKsteps];      // rebuild image e: rope_blocks columns [kst_src[e], kst_src[e] + 16)
   // per group: first and last 16-column step holding its RoPE coordinates, and the image of the first step (the
   // steps of a group are consecutive images)
   int rope_ks0[4], rope_ks1[4], rope_e0[4];
