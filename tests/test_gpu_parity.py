@@ -535,6 +535,26 @@ def test_decode_learned_ranks(r_k, page):
     assert_close_out(out, exp, f"r_k {r_k}, page {page}")
 
 
+@pytest.mark.parametrize("k_ranks,r_v,rope_align", [
+    ((16, 16, 16, 16), 64, False),      # one chunk holds four groups' RoPE runs: the per-step rebuild words
+    ((24, 8, 40, 16), 96, False),       # runs of two groups meeting inside a 16-column step
+    ((96, 112, 144, 160), 512, True),   # rope-aligned: whole-chunk runs, then chunks without RoPE coordinates
+])
+def test_decode_rebuild_issue_paths(k_ranks, r_v, rope_align):
+    """The decode issuer's three ways of issuing the RoPE-key rebuild (the host encodes each key chunk's rebuild steps
+    as runs when they form at most two, a whole-chunk run issued straight; otherwise per step), against the fp32
+    oracle."""
+    spec = synth.LayerSpec(tuple(k_ranks), r_v, 1024, rope_align=rope_align)
+    w = synth.make_layer(spec)
+    lat, ref = layer_pair(w, max_pos=3000)
+    seqs = [1500, 129, 2049, 7]
+    batch = synth.make_batch(w.layout, seqs, page=16, seed=31)
+    q = synth.make_queries(len(seqs), seed=32)
+    out, *_ = run_decode(lat, q.to(DEV), batch.cache.to(DEV), batch.block_table.to(DEV), batch.seq_lens.to(DEV))
+    exp = oracle.decode_fp32(q, batch.cache, batch.block_table, batch.seq_lens, ref, SCALE)
+    assert_close_out(out, exp, f"ranks {k_ranks}, r_v {r_v}, rope_align {rope_align}")
+
+
 def test_decode_invariances():
     """Bit-identical under a permutation of physical blocks; within tolerance across different CTA counts."""
     spec = synth.spec_from_ranks(448, 576)
