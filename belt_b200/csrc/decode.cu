@@ -478,11 +478,11 @@ __global__ void __launch_bounds__(dec::kThreads, 1)
       auto wait = [&](int bar, uint32_t parity) -> bool {
         return mbar_wait(&bars[bar], parity, abort_flag, p.err, kErrTimeoutMma);
       };
+      // No tcgen05 fence after a stage's full barrier: its data was written by TMA (async proxy, completed through the
+      // barrier's transaction count), not by threads whose tcgen05 operations need ordering.
       auto full = [&](int& st) -> bool {
         st = slot;
-        if (!wait(bFull + st, slot_par)) return false;
-        tc_fence_after();
-        return true;
+        return wait(bFull + st, slot_par);
       };
       auto release = [&](int st) {   // the stage's MMAs are all issued: its slot is free once they complete
         mma_commit(&bars[bEmpty + st]);
