@@ -28,6 +28,8 @@ namespace {
 constexpr int kPwThreads = 128;
 constexpr int kPwXBytes = 128 * 128;                  // 128 tokens x 64 hidden
 constexpr int kPwChunkBytes = 64 * 128;               // 64 rows x 64 hidden
+// Phase-1 ring of 3 stages of the widest window (x tile + 5 chunks). Stages sized to the item's window (4-7 stages in
+// 224 KB) were measured no faster: phase 1 is bound by the SM's inflow of 128-byte rows (~70 GB/s), not by latency.
 constexpr int kPwStage = kPwXBytes + kPwMaxChunks * kPwChunkBytes;   // 56 KB
 constexpr int kPwStages = 3;
 constexpr int kPwRing = kPwStages * kPwStage;
@@ -65,7 +67,21 @@ __global__ void __launch_bounds__(kPwThreads, 1)
   // the group's two runs in registers (the epilogues test many columns; the arrays are indexed by the item)
   const int a_lo = group ? p.a_lo[g] : 0, a_hi = group ? a_lo + p.a_n[g] : 0;
   const int b_lo = group ? p.b_lo[g] : 0, b_hi = group ? b_lo + p.b_n[g] : 0;
-  auto in_runs = [&](int col) { return (col >= a_lo && col < a_hi) || (col >= b_lo && col < b_hi); };
+  // Bit j set: column cb + j of a 32-column window lies in one of the group's runs. The window is the same for every
+  // thread, so the mask is computed once per window and applied to the packed words without a branch per column (a
+  // test per column cost ~1,500 cycles per window, most of epilogue 1).
+  auto run_mask = [&](int cb) -> uint32_t {
+    auto span = [&](int lo, int hi) -> uint32_t {
+      const int l = max(lo - cb, 0), h = min(hi - cb, 32);
+      if (h <= l) return 0u;
+      return (h - l == 32 ? 0xFFFFFFFFu : (1u << (h - l)) - 1u) << l;
+    };
+    return span(a_lo, a_hi) | span(b_lo, b_hi);
+  };
+  // the packed word j (columns cb + 2j, cb + 2j + 1) with the halves outside the runs zeroed
+  auto keep_word = [](uint32_t m, int j) -> uint32_t {
+    return ((0u - ((m >> (2 * j)) & 1u)) & 0x0000FFFFu) | ((0u - ((m >> (2 * j + 1)) & 1u)) & 0xFFFF0000u);
+  };
   const int nch = p.item_nch[item];
   const int win_lo = p.item_chunk[item][0];
   const bool win_contig = p.item_chunk[item][nch - 1] - win_lo == nch - 1;
@@ -188,26 +204,17 @@ __global__ void __launch_bounds__(kPwThreads, 1)
             }
           }
           if (group) {
+            const uint32_t m = run_mask(cb);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int c = cb + 2 * j;
-              if (!in_runs(c)) pk[j] &= 0xFFFF0000u;
-              if (!in_runs(c + 1)) pk[j] &= 0x0000FFFFu;
-            }
+            for (int j = 0; j < 16; ++j) pk[j] &= keep_word(m, j);
           }
         } else {
           tmem_ld32(tmem + lane_base + 64 * i + 32 * half, v);
           tmem_ld_wait();
+          const uint32_t m = group ? run_mask(cb) : 0xFFFFFFFFu;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
-            if (group) {
-              const int c = cb + 2 * j;
-              if (!in_runs(c)) lo = 0.f;
-              if (!in_runs(c + 1)) hi = 0.f;
-            }
-            pk[j] = pack_bf16(lo, hi);
-          }
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])) & keep_word(m, j);
         }
         if (group) {
           uint8_t* a2 = smem + kPwA2 + i * kPwXBytes;
@@ -281,14 +288,17 @@ __global__ void __launch_bounds__(kPwThreads, 1)
     tc_fence_after();
     // ---------------------------------------------------------------- epilogue 2: rho, scaled runs
     if (done2 && !*abort_flag) {
-      float ss = 0.f;
+      // sum of squares over the 256 channels in four interleaved partial sums (one dependent chain of 256 FMAs was
+      // ~1,000 cycles of latency)
+      float ss4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t v[32];
       for (int c0 = 0; c0 < kD; c0 += 32) {
         tmem_ld32(tmem + lane_base + c0, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ss = fmaf(__uint_as_float(v[j]), __uint_as_float(v[j]), ss);
+        for (int j = 0; j < 32; ++j) ss4[j & 3] = fmaf(__uint_as_float(v[j]), __uint_as_float(v[j]), ss4[j & 3]);
       }
+      const float ss = (ss4[0] + ss4[1]) + (ss4[2] + ss4[3]);
       const float inv = rsqrtf(ss / kD + p.eps);
       if (dst) {
         const uint8_t* a2 = smem + kPwA2;
